@@ -1,0 +1,220 @@
+"""Torch-facing wrappers of the four C-ABI entry points.
+
+Every function takes CUDA tensors, launches on the current torch stream and
+returns without synchronising (unless ``check_status=True``, which reads the
+device status word and raises on a device-side error). Workspaces come from
+torch's caching allocator unless the caller passes one.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Optional
+
+import torch
+
+from . import _lib
+from ._lib import A11Error, check, lib
+
+
+def _ptr(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(t: torch.Tensor, name: str, dtype=None, device=None):
+    if not t.is_cuda:
+        raise A11Error(_lib.EINVAL, f"{name} must be a CUDA tensor")
+    if not t.is_contiguous():
+        raise A11Error(_lib.EINVAL, f"{name} must be contiguous")
+    if dtype is not None and t.dtype != dtype:
+        raise A11Error(_lib.EINVAL, f"{name} must be {dtype}, got {t.dtype}")
+
+
+def read_status(workspace: torch.Tensor):
+    """(code, detail) of the device status word; synchronises the stream."""
+    st, de = _lib.C.c_int32(0), _lib.C.c_int32(0)
+    check(lib.a11s_read_status(workspace.data_ptr(), _lib.C.byref(st), _lib.C.byref(de), _stream()))
+    return int(st.value), int(de.value)
+
+
+def raise_on_status(workspace: torch.Tensor) -> None:
+    code, detail = read_status(workspace)
+    if code != _lib.OK:
+        raise A11Error(code, f"device status (detail {detail})")
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+# --------------------------------------------------------------------------- K3
+@dataclass
+class AcceptResult:
+    accept_len: torch.Tensor       # int32 [B]
+    accepted_nodes: torch.Tensor   # int32 [B, N]
+    accepted_tokens: torch.Tensor  # int32 [B, N]
+    bonus: torch.Tensor            # int32 [B]
+    node_probs: Optional[torch.Tensor]
+    workspace: torch.Tensor
+
+
+def accept_workspace_bytes(mode: int, batch: int, max_nodes: int, vocab: int) -> int:
+    return int(lib.a11s_accept_workspace_bytes(mode, batch, max_nodes, vocab))
+
+
+def accept(mode: int, target_logits: torch.Tensor, tokens: torch.Tensor, parents: torch.Tensor,
+           n_nodes: Optional[torch.Tensor] = None, draft_logits: Optional[torch.Tensor] = None,
+           temperature: float = 1.0, uniforms: Optional[torch.Tensor] = None,
+           stats: Optional[torch.Tensor] = None, want_node_probs: bool = False,
+           ws: Optional[torch.Tensor] = None, out: Optional[AcceptResult] = None,
+           check_status: bool = False) -> AcceptResult:
+    """K3. target_logits [B, N, V] (fp32 or bf16, rows contiguous)."""
+    B, N, V = target_logits.shape
+    dt = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}.get(target_logits.dtype)
+    if dt is None:
+        raise A11Error(_lib.EINVAL, "logits must be float32 or bfloat16")
+    _need(target_logits, "target_logits")
+    _need(tokens, "tokens", torch.int32)
+    _need(parents, "parents", torch.int32)
+    if n_nodes is not None:
+        _need(n_nodes, "n_nodes", torch.int32)
+    if draft_logits is not None:
+        _need(draft_logits, "draft_logits", target_logits.dtype)
+        if draft_logits.shape != target_logits.shape:
+            raise A11Error(_lib.EINVAL, "draft_logits shape differs from target_logits")
+    if uniforms is not None:
+        _need(uniforms, "uniforms", torch.float32)
+    dev = target_logits.device
+    if out is None:
+        out = AcceptResult(
+            accept_len=torch.empty(B, dtype=torch.int32, device=dev),
+            accepted_nodes=torch.empty(B, N, dtype=torch.int32, device=dev),
+            accepted_tokens=torch.empty(B, N, dtype=torch.int32, device=dev),
+            bonus=torch.empty(B, dtype=torch.int32, device=dev),
+            node_probs=torch.empty(B, N, dtype=torch.float32, device=dev) if want_node_probs else None,
+            workspace=ws if ws is not None else workspace(accept_workspace_bytes(mode, B, N, V), dev))
+    rc = lib.a11s_accept(mode, dt, target_logits.data_ptr(), _ptr(draft_logits), V,
+                         float(temperature), _ptr(uniforms), tokens.data_ptr(), parents.data_ptr(),
+                         _ptr(n_nodes), B, N, V, out.accept_len.data_ptr(),
+                         out.accepted_nodes.data_ptr(), out.accepted_tokens.data_ptr(),
+                         out.bonus.data_ptr(), _ptr(out.node_probs), _ptr(stats),
+                         out.workspace.data_ptr(), out.workspace.numel(), _stream())
+    check(rc)
+    if check_status:
+        raise_on_status(out.workspace)
+    return out
+
+
+# --------------------------------------------------------------------------- K2
+def tree_attention_workspace_bytes(batch, max_nodes, num_q_heads, num_kv_heads, head_dim, max_kv_len):
+    return int(lib.a11s_tree_attention_workspace_bytes(batch, max_nodes, num_q_heads, num_kv_heads,
+                                                       head_dim, max_kv_len))
+
+
+def tree_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                   page_table: torch.Tensor, ctx_lens: torch.Tensor, parents: torch.Tensor,
+                   n_nodes: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                   max_kv_len: Optional[int] = None, want_lse: bool = False,
+                   out: Optional[torch.Tensor] = None, lse: Optional[torch.Tensor] = None,
+                   ws: Optional[torch.Tensor] = None, check_status: bool = False):
+    """K2. q [B, N, Hq, D] bf16; pools [P, 16, Hkv, D] bf16; page_table [B, maxpages] int32."""
+    B, N, Hq, D = q.shape
+    P, pg, Hkv, D2 = k_pool.shape
+    if pg != _lib.PAGE_TOKENS or D2 != D or v_pool.shape != k_pool.shape:
+        raise A11Error(_lib.EINVAL, "pool shape must be [P, 16, Hkv, D] for K and V")
+    for t, nm in ((q, "q"), (k_pool, "k_pool"), (v_pool, "v_pool")):
+        _need(t, nm, torch.bfloat16)
+    _need(page_table, "page_table", torch.int32)
+    _need(ctx_lens, "ctx_lens", torch.int32)
+    _need(parents, "parents", torch.int32)
+    if max_kv_len is None:
+        max_kv_len = page_table.shape[1] * _lib.PAGE_TOKENS
+    if scale is None:
+        scale = 1.0 / math.sqrt(D)
+    dev = q.device
+    if out is None:
+        out = torch.empty_like(q)
+    if want_lse and lse is None:
+        lse = torch.empty(B, N, Hq, dtype=torch.float32, device=dev)
+    if ws is None:
+        ws = workspace(tree_attention_workspace_bytes(B, N, Hq, Hkv, D, max_kv_len), dev)
+    rc = lib.a11s_tree_attention(q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), P,
+                                 page_table.data_ptr(), page_table.shape[1], ctx_lens.data_ptr(),
+                                 parents.data_ptr(), _ptr(n_nodes), B, N, Hq, Hkv, D, int(max_kv_len),
+                                 float(scale), out.data_ptr(), _ptr(lse), ws.data_ptr(), ws.numel(),
+                                 _stream())
+    check(rc)
+    if check_status:
+        raise_on_status(ws)
+    return out, lse, ws
+
+
+# --------------------------------------------------------------------------- K4
+def kv_compact(k_pool: torch.Tensor, v_pool: torch.Tensor, page_table: torch.Tensor,
+               seq_lens: torch.Tensor, accept_len: torch.Tensor, accepted_nodes: torch.Tensor,
+               n_nodes: Optional[torch.Tensor] = None, num_layers: int = 1,
+               freed_pages: Optional[torch.Tensor] = None, n_freed: Optional[torch.Tensor] = None,
+               ws: Optional[torch.Tensor] = None, check_status: bool = False):
+    """K4, in place on the pools, page_table and seq_lens.
+
+    Pools are [P, 16, Hkv, D] (or [layers, P, 16, Hkv, D] with num_layers > 1).
+    """
+    for t, nm in ((page_table, "page_table"), (seq_lens, "seq_lens"), (accept_len, "accept_len"),
+                  (accepted_nodes, "accepted_nodes")):
+        _need(t, nm, torch.int32)
+    _need(k_pool, "k_pool")
+    _need(v_pool, "v_pool")
+    B, N = accepted_nodes.shape
+    shape = k_pool.shape[1:] if num_layers > 1 else k_pool.shape
+    P, row_elems = shape[0], shape[2] * shape[3]
+    layer_stride = P * _lib.PAGE_TOKENS * row_elems if num_layers > 1 else 0
+    dev = k_pool.device
+    if freed_pages is None:
+        freed_pages = torch.full_like(page_table, -1)
+    if n_freed is None:
+        n_freed = torch.zeros(B, dtype=torch.int32, device=dev)
+    if ws is None:
+        ws = workspace(256, dev)
+    rc = lib.a11s_kv_compact(k_pool.data_ptr(), v_pool.data_ptr(), num_layers, layer_stride, P,
+                             row_elems, k_pool.element_size(), page_table.data_ptr(),
+                             page_table.shape[1], seq_lens.data_ptr(), accept_len.data_ptr(),
+                             accepted_nodes.data_ptr(), _ptr(n_nodes), B, N, freed_pages.data_ptr(),
+                             n_freed.data_ptr(), ws.data_ptr(), ws.numel(), _stream())
+    check(rc)
+    if check_status:
+        raise_on_status(ws)
+    return freed_pages, n_freed
+
+
+# --------------------------------------------------------------------------- K1
+def ngram_bucket(a: int, b: int, log2_buckets: int) -> int:
+    return int(lib.a11s_ngram_bucket(a, b, log2_buckets))
+
+
+def ngram_expand(table: torch.Tensor, last_tokens: torch.Tensor, width_root: int = 4,
+                 width_inner: int = 2, max_depth: int = 5, max_nodes: int = 64, out=None):
+    """K1. table int32 [2^k, slots, 2]; last_tokens int32 [B, 2]. Returns
+    (tokens, parents, depths, n_nodes)."""
+    _need(table, "table", torch.int32)
+    _need(last_tokens, "last_tokens", torch.int32)
+    nb, slots, two = table.shape
+    log2b = nb.bit_length() - 1
+    if two != 2 or (1 << log2b) != nb:
+        raise A11Error(_lib.EINVAL, "table must be [2^k, slots, 2]")
+    B = last_tokens.shape[0]
+    dev = table.device
+    if out is None:
+        out = (torch.empty(B, max_nodes, dtype=torch.int32, device=dev),
+               torch.empty(B, max_nodes, dtype=torch.int32, device=dev),
+               torch.empty(B, max_nodes, dtype=torch.int32, device=dev),
+               torch.empty(B, dtype=torch.int32, device=dev))
+    tk, pa, de, nn = out
+    rc = lib.a11s_ngram_expand(table.data_ptr(), log2b, slots, last_tokens.data_ptr(), B,
+                               width_root, width_inner, max_depth, max_nodes, tk.data_ptr(),
+                               pa.data_ptr(), de.data_ptr(), nn.data_ptr(), _stream())
+    check(rc)
+    return out

@@ -1,0 +1,329 @@
+// api.cu - the extern "C" boundary of liba11spec.so (declared in include/a11spec.h).
+//
+// Host-side validation, workspace carving and launches. Nothing here allocates
+// device memory or synchronises a stream (except a11s_read_status, documented
+// as synchronising).
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char *fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_err = buf;
+    return code;
+}
+
+int cuda_fail(cudaError_t e, const char *what) {
+    return fail(A11S_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
+
+constexpr size_t kHeaderBytes = 256;  // status word lives at offset 0
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+            n = 148;
+    }
+    return n;
+}
+
+// ---- acceptance workspace layout ----
+struct AcceptLayout {
+    size_t counters, recs, total;
+};
+AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
+    AcceptLayout L;
+    const size_t nch = (size_t)(vocab + A11S_CHUNK - 1) / A11S_CHUNK;
+    const size_t rows = (size_t)batch * max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    L.counters = kHeaderBytes;
+    L.recs = L.counters + up256(sizeof(int32_t) * (size_t)batch);
+    L.total = L.recs + up256(rows * nch * sizeof(a11s::ChunkRec));
+    return L;
+}
+
+}  // namespace
+
+extern "C" {
+
+int a11s_abi_version(void) { return A11S_ABI_VERSION; }
+
+const char *a11s_last_error(void) { return g_err.c_str(); }
+
+int a11s_read_status(const void *workspace, int32_t *status, int32_t *detail, void *stream) {
+    if (!workspace || !status) return fail(A11S_EINVAL, "a11s_read_status: null argument");
+    a11s::StatusWord w{};
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemcpyAsync(&w, workspace, sizeof w, cudaMemcpyDeviceToHost, s);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_read_status");
+    *status = w.code;
+    if (detail) *detail = w.code ? w.detail : -1;
+    return A11S_OK;
+}
+
+// ------------------------------------------------------------------- K3
+size_t a11s_accept_workspace_bytes(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
+    if (batch < 0 || max_nodes < 1 || vocab < 1) return 0;
+    return accept_layout(mode, batch, max_nodes, vocab).total;
+}
+
+int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const void *draft_logits,
+                int64_t row_stride, float temperature, const float *uniforms,
+                const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes,
+                int32_t batch, int32_t max_nodes, int32_t vocab, int32_t *accept_len,
+                int32_t *accepted_nodes, int32_t *accepted_tokens, int32_t *bonus,
+                float *node_probs, int64_t *stats, void *workspace, size_t workspace_bytes,
+                void *stream) {
+    if (mode < A11S_ACCEPT_GREEDY || mode > A11S_ACCEPT_STOCH_DRAFT)
+        return fail(A11S_EINVAL, "a11s_accept: unknown mode %d", mode);
+    if (dtype != A11S_F32 && dtype != A11S_BF16)
+        return fail(A11S_EINVAL, "a11s_accept: unknown dtype %d", dtype);
+    if (batch < 0) return fail(A11S_EINVAL, "a11s_accept: batch %d < 0", batch);
+    if (max_nodes < 1 || max_nodes > A11S_MAX_NODES)
+        return fail(A11S_EUNSUPPORTED, "a11s_accept: max_nodes %d outside [1, %d]", max_nodes,
+                    A11S_MAX_NODES);
+    if (vocab < 1 || vocab > A11S_MAX_VOCAB)
+        return fail(A11S_EUNSUPPORTED, "a11s_accept: vocab %d outside [1, %d]", vocab, A11S_MAX_VOCAB);
+    const int vec = dtype == A11S_BF16 ? 8 : 4;
+    if (row_stride < vocab || row_stride % vec || vocab % vec)
+        return fail(A11S_EINVAL,
+                    "a11s_accept: row_stride %lld and vocab %d must be multiples of %d, stride >= vocab",
+                    (long long)row_stride, vocab, vec);
+    if (batch == 0) return A11S_OK;
+    if (!target_logits || !tokens || !parents || !accept_len || !accepted_nodes ||
+        !accepted_tokens || !bonus || !workspace)
+        return fail(A11S_EINVAL, "a11s_accept: null required pointer");
+    if (!aligned16(target_logits) || (draft_logits && !aligned16(draft_logits)))
+        return fail(A11S_EINVAL, "a11s_accept: logits must be 16-byte aligned");
+    if (mode != A11S_ACCEPT_GREEDY) {
+        if (!uniforms) return fail(A11S_EINVAL, "a11s_accept: sampling modes need uniforms");
+        if (!(temperature > 0.0f) || !std::isfinite(temperature))
+            return fail(A11S_EINVAL, "a11s_accept: temperature must be finite and > 0");
+    }
+    if (mode == A11S_ACCEPT_STOCH_DRAFT && !draft_logits)
+        return fail(A11S_EINVAL, "a11s_accept: STOCH_DRAFT needs draft_logits");
+    if (!aligned16(workspace)) return fail(A11S_EINVAL, "a11s_accept: workspace must be 16-byte aligned");
+    const AcceptLayout L = accept_layout(mode, batch, max_nodes, vocab);
+    if (workspace_bytes < L.total)
+        return fail(A11S_ENOSPACE, "a11s_accept: workspace %zu < %zu bytes", workspace_bytes, L.total);
+
+    a11s::AcceptArgs a{};
+    a.target = target_logits;
+    a.draft = draft_logits;
+    a.stride = row_stride;
+    const double t = temperature < 1e-5f ? 1e-5 : (double)temperature;  // engine/sampler.py:10
+    a.k = (float)(1.4426950408889634 / t);
+    a.uniforms = uniforms;
+    a.tokens = tokens;
+    a.parents = parents;
+    a.n_nodes = n_nodes;
+    a.B = batch;
+    a.N = max_nodes;
+    a.V = vocab;
+    a.nch = (vocab + A11S_CHUNK - 1) / A11S_CHUNK;
+    a.rows_per_seq = max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    a.units_per_seq = a.rows_per_seq * a.nch;
+    a.accept_len = accept_len;
+    a.acc_nodes = accepted_nodes;
+    a.acc_tokens = accepted_tokens;
+    a.bonus = bonus;
+    a.node_probs = mode == A11S_ACCEPT_GREEDY ? nullptr : node_probs;
+    a.stats = reinterpret_cast<long long *>(stats);
+    char *ws = static_cast<char *>(workspace);
+    a.status = reinterpret_cast<a11s::StatusWord *>(ws);
+    a.counters = reinterpret_cast<int32_t *>(ws + L.counters);
+    a.recs = reinterpret_cast<a11s::ChunkRec *>(ws + L.recs);
+
+    // Balance: about 4 waves of 3 resident 256-thread blocks per SM, at least
+    // 8 chunks (one per warp) per block.
+    const long long total_units = (long long)batch * a.units_per_seq;
+    const long long target_blocks = (long long)sm_count() * 3 * 4;
+    long long slice = (total_units + target_blocks - 1) / target_blocks;
+    slice = ((slice + 7) / 8) * 8;
+    if (slice < 8) slice = 8;
+    if (slice > a.units_per_seq) slice = a.units_per_seq;
+    a.slice = (int32_t)slice;
+    const int grid_x = (a.units_per_seq + a.slice - 1) / a.slice;
+
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ws, 0, L.recs, s);  // status word + per-sequence counters
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: clearing workspace");
+    e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_x, s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: launch");
+    return A11S_OK;
+}
+
+// ------------------------------------------------------------------- K4
+int a11s_kv_compact(void *k_pool, void *v_pool, int32_t num_layers, int64_t layer_stride,
+                    int32_t num_pages, int32_t row_elems, int32_t elem_bytes, int32_t *page_table,
+                    int32_t max_pages_per_seq, int32_t *seq_lens, const int32_t *accept_len,
+                    const int32_t *accepted_nodes, const int32_t *n_nodes, int32_t batch,
+                    int32_t max_nodes, int32_t *freed_pages, int32_t *n_freed, void *workspace,
+                    size_t workspace_bytes, void *stream) {
+    if (batch < 0 || num_layers < 1 || num_pages < 1 || row_elems < 1 || max_nodes < 1 ||
+        max_pages_per_seq < 1)
+        return fail(A11S_EINVAL, "a11s_kv_compact: non-positive size");
+    if (elem_bytes != 2 && elem_bytes != 4)
+        return fail(A11S_EINVAL, "a11s_kv_compact: elem_bytes must be 2 or 4");
+    const int64_t row_bytes = (int64_t)row_elems * elem_bytes;
+    if (row_bytes % 16) return fail(A11S_EINVAL, "a11s_kv_compact: row bytes %lld not a multiple of 16",
+                                    (long long)row_bytes);
+    const int64_t slab = (int64_t)num_pages * A11S_PAGE_TOKENS * row_elems;
+    if (num_layers > 1 && layer_stride < slab)
+        return fail(A11S_EINVAL, "a11s_kv_compact: layer_stride smaller than one layer");
+    if (batch == 0) return A11S_OK;
+    if (!k_pool || !v_pool || !page_table || !seq_lens || !accept_len || !accepted_nodes)
+        return fail(A11S_EINVAL, "a11s_kv_compact: null required pointer");
+    if (!aligned16(k_pool) || !aligned16(v_pool))
+        return fail(A11S_EINVAL, "a11s_kv_compact: pools must be 16-byte aligned");
+    if (workspace && workspace_bytes < sizeof(a11s::StatusWord))
+        return fail(A11S_ENOSPACE, "a11s_kv_compact: workspace too small for the status word");
+    a11s::CompactArgs a{};
+    a.k_pool = static_cast<char *>(k_pool);
+    a.v_pool = static_cast<char *>(v_pool);
+    a.num_layers = num_layers;
+    a.layer_stride_bytes = (num_layers > 1 ? layer_stride : slab) * elem_bytes;
+    a.num_pages = num_pages;
+    a.row_bytes = (int32_t)row_bytes;
+    a.page_table = page_table;
+    a.max_pages = max_pages_per_seq;
+    a.seq_lens = seq_lens;
+    a.accept_len = accept_len;
+    a.accepted_nodes = accepted_nodes;
+    a.n_nodes = n_nodes;
+    a.B = batch;
+    a.N = max_nodes;
+    a.freed_pages = freed_pages;
+    a.n_freed = n_freed;
+    a.status = static_cast<a11s::StatusWord *>(workspace);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    if (workspace) {
+        cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(a11s::StatusWord), s);
+        if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_compact: clearing status");
+    }
+    cudaError_t e = a11s::launch_kv_compact(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_compact: launch");
+    return A11S_OK;
+}
+
+// ------------------------------------------------------------------- K1
+uint32_t a11s_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets) {
+    uint64_t z = ((uint64_t)(uint32_t)a << 32) | (uint32_t)b;
+    z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+    z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+    z ^= z >> 31;
+    return (uint32_t)(z >> (64 - log2_buckets));
+}
+
+int a11s_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
+                      const int32_t *last_tokens, int32_t batch, int32_t width_root,
+                      int32_t width_inner, int32_t max_depth, int32_t max_nodes, int32_t *tokens,
+                      int32_t *parents, int32_t *depths, int32_t *n_nodes, void *stream) {
+    if (log2_buckets < 1 || log2_buckets > 30)
+        return fail(A11S_EINVAL, "a11s_ngram_expand: log2_buckets %d outside [1, 30]", log2_buckets);
+    if (slots < 1 || slots > 32) return fail(A11S_EUNSUPPORTED, "a11s_ngram_expand: slots %d outside [1, 32]", slots);
+    if (width_root < 0 || width_inner < 0 || width_root > slots || width_inner > slots)
+        return fail(A11S_EINVAL, "a11s_ngram_expand: widths must lie in [0, slots]");
+    if (max_depth < 0 || max_nodes < 1 || max_nodes > A11S_MAX_NODES)
+        return fail(A11S_EINVAL, "a11s_ngram_expand: bad max_depth / max_nodes");
+    if (batch < 0) return fail(A11S_EINVAL, "a11s_ngram_expand: batch < 0");
+    if (batch == 0) return A11S_OK;
+    if (!table || !last_tokens || !tokens || !parents || !depths || !n_nodes)
+        return fail(A11S_EINVAL, "a11s_ngram_expand: null required pointer");
+    a11s::NgramArgs a{table, log2_buckets, slots, last_tokens, batch, width_root, width_inner,
+                      max_depth, max_nodes, tokens, parents, depths, n_nodes};
+    cudaError_t e = a11s::launch_ngram_expand(a, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_ngram_expand: launch");
+    return A11S_OK;
+}
+
+// ------------------------------------------------------------------- K2
+size_t a11s_tree_attention_workspace_bytes(int32_t batch, int32_t max_nodes, int32_t num_q_heads,
+                                           int32_t num_kv_heads, int32_t head_dim,
+                                           int32_t max_kv_len) {
+    if (batch < 0 || max_nodes < 1 || num_q_heads < 1 || num_kv_heads < 1 || head_dim < 1)
+        return 0;
+    const int splits = a11s::tree_attention_splits(batch, max_nodes, num_q_heads, num_kv_heads, max_kv_len);
+    return kHeaderBytes + up256(a11s::tree_attention_partials_bytes(batch, max_nodes, num_q_heads,
+                                                                    head_dim, splits));
+}
+
+int a11s_tree_attention(const void *q, const void *k_pool, const void *v_pool, int32_t num_pages,
+                        const int32_t *page_table, int32_t max_pages_per_seq,
+                        const int32_t *ctx_lens, const int32_t *parents, const int32_t *n_nodes,
+                        int32_t batch, int32_t max_nodes, int32_t num_q_heads,
+                        int32_t num_kv_heads, int32_t head_dim, int32_t max_kv_len, float scale,
+                        void *out, float *lse, void *workspace, size_t workspace_bytes,
+                        void *stream) {
+    if (head_dim != 128) return fail(A11S_EUNSUPPORTED, "a11s_tree_attention: head_dim %d != 128", head_dim);
+    if (num_kv_heads < 1 || num_q_heads != 8 * num_kv_heads)
+        return fail(A11S_EUNSUPPORTED, "a11s_tree_attention: needs num_q_heads == 8 * num_kv_heads");
+    if (max_nodes < 1 || max_nodes > 64)
+        return fail(A11S_EUNSUPPORTED, "a11s_tree_attention: max_nodes %d outside [1, 64]", max_nodes);
+    if (batch < 0 || num_pages < 1 || max_pages_per_seq < 1 || max_kv_len < 1)
+        return fail(A11S_EINVAL, "a11s_tree_attention: non-positive size");
+    if ((int64_t)max_pages_per_seq * A11S_PAGE_TOKENS < max_kv_len)
+        return fail(A11S_EINVAL, "a11s_tree_attention: page table shorter than max_kv_len");
+    if (!(scale > 0.0f) || !std::isfinite(scale)) return fail(A11S_EINVAL, "a11s_tree_attention: bad scale");
+    if (batch == 0) return A11S_OK;
+    if (!q || !k_pool || !v_pool || !page_table || !ctx_lens || !parents || !out || !workspace)
+        return fail(A11S_EINVAL, "a11s_tree_attention: null required pointer");
+    if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) || !aligned16(workspace))
+        return fail(A11S_EINVAL, "a11s_tree_attention: tensors must be 16-byte aligned");
+    const size_t need = a11s_tree_attention_workspace_bytes(batch, max_nodes, num_q_heads, num_kv_heads,
+                                                            head_dim, max_kv_len);
+    if (workspace_bytes < need)
+        return fail(A11S_ENOSPACE, "a11s_tree_attention: workspace %zu < %zu bytes", workspace_bytes, need);
+    a11s::AttnArgs a{};
+    a.q = q;
+    a.k_pool = k_pool;
+    a.v_pool = v_pool;
+    a.num_pages = num_pages;
+    a.page_table = page_table;
+    a.max_pages = max_pages_per_seq;
+    a.ctx_lens = ctx_lens;
+    a.parents = parents;
+    a.n_nodes = n_nodes;
+    a.B = batch;
+    a.N = max_nodes;
+    a.Hq = num_q_heads;
+    a.Hkv = num_kv_heads;
+    a.D = head_dim;
+    a.max_kv_len = max_kv_len;
+    a.scale = scale;
+    a.out = out;
+    a.lse = lse;
+    char *ws = static_cast<char *>(workspace);
+    a.status = reinterpret_cast<a11s::StatusWord *>(ws);
+    a.splits = a11s::tree_attention_splits(batch, max_nodes, num_q_heads, num_kv_heads, max_kv_len);
+    a.part_o = reinterpret_cast<float *>(ws + kHeaderBytes);
+    a.part_ml = a.part_o + (size_t)a.splits * batch * max_nodes * num_q_heads * head_dim;
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(ws, 0, sizeof(a11s::StatusWord), s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_tree_attention: clearing status");
+    e = a11s::launch_tree_attention(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_tree_attention: launch");
+    return A11S_OK;
+}
+
+}  // extern "C"

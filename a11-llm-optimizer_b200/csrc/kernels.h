@@ -1,0 +1,98 @@
+// kernels.h - internal launch interfaces between the C ABI (api.cu) and the kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace a11s {
+
+struct StatusWord;
+
+// 16-byte record of one 2048-token chunk of one logits row.
+// greedy: cmax = chunk max, aux = argmax token (lowest index on ties);
+// sampling: cmax = chunk max, aux = frame c_j (INT32_MIN if all -inf), sum = S_j.
+struct __align__(16) ChunkRec {
+    float cmax;
+    int32_t aux;
+    unsigned long long sum;
+};
+
+struct AcceptArgs {
+    const void *target;
+    const void *draft;
+    int64_t stride;  // elements between rows
+    float k;         // log2(e) / max(T, 1e-5), rounded to float on the host
+    const float *uniforms;
+    const int32_t *tokens;
+    const int32_t *parents;
+    const int32_t *n_nodes;
+    int32_t B, N, V, nch, rows_per_seq, units_per_seq, slice;
+    int32_t *accept_len;
+    int32_t *acc_nodes;
+    int32_t *acc_tokens;
+    int32_t *bonus;
+    float *node_probs;
+    long long *stats;
+    ChunkRec *recs;
+    int32_t *counters;
+    StatusWord *status;
+};
+
+cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_x, cudaStream_t s);
+
+struct CompactArgs {
+    char *k_pool;
+    char *v_pool;
+    int32_t num_layers;
+    int64_t layer_stride_bytes;
+    int32_t num_pages;
+    int32_t row_bytes;
+    int32_t *page_table;
+    int32_t max_pages;
+    int32_t *seq_lens;
+    const int32_t *accept_len;
+    const int32_t *accepted_nodes;
+    const int32_t *n_nodes;
+    int32_t B, N;
+    int32_t *freed_pages;
+    int32_t *n_freed;
+    StatusWord *status;
+};
+
+cudaError_t launch_kv_compact(const CompactArgs &a, cudaStream_t s);
+
+struct NgramArgs {
+    const int32_t *table;
+    int32_t log2_buckets, slots;
+    const int32_t *last_tokens;
+    int32_t B, width_root, width_inner, max_depth, max_nodes;
+    int32_t *tokens, *parents, *depths, *n_nodes;
+};
+
+cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s);
+
+struct AttnArgs {
+    const void *q;
+    const void *k_pool;
+    const void *v_pool;
+    int32_t num_pages;
+    const int32_t *page_table;
+    int32_t max_pages;
+    const int32_t *ctx_lens;
+    const int32_t *parents;
+    const int32_t *n_nodes;
+    int32_t B, N, Hq, Hkv, D, max_kv_len;
+    float scale;
+    void *out;
+    float *lse;
+    // split-KV partials (workspace)
+    float *part_o;    // [splits][B][N][Hq][D]
+    float *part_ml;   // [splits][B][N][Hq][2]  (running max in log2 units, sum)
+    int32_t splits, kv_per_split;
+    StatusWord *status;
+};
+
+cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s);
+size_t tree_attention_partials_bytes(int32_t B, int32_t N, int32_t Hq, int32_t D, int32_t splits);
+int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t max_kv_len);
+
+}  // namespace a11s

@@ -1,0 +1,225 @@
+/*
+ * a11spec.h - C ABI of the B200 speculative-decoding hot path.
+ *
+ * Four device steps, one entry point each, all asynchronous on the caller's
+ * CUDA stream (passed as `void *stream`, a cudaStream_t; NULL = legacy
+ * default stream):
+ *
+ *   a11s_ngram_expand     hashed trigram table  -> draft token tree      (K1)
+ *   a11s_tree_attention   tree-masked attention over 16-token KV pages   (K2)
+ *   a11s_accept           vocab softmax/argmax + acceptance + bonus draw  (K3)
+ *   a11s_kv_compact       move the accepted path's KV, shrink page tables (K4)
+ *
+ * Conventions shared by every entry point
+ *   - All tensor arguments are caller-owned DEVICE pointers, row-major and
+ *     densely packed unless a stride argument says otherwise. Nothing here
+ *     allocates device memory or synchronises the stream. Scratch memory is the
+ *     caller's `workspace`, sized by the matching *_workspace_bytes() call.
+ *   - Return value: A11S_OK when the arguments were valid and the kernels were
+ *     enqueued; otherwise an A11S_E* code and a message in a11s_last_error().
+ *     Errors found on the device (a token id >= vocab, a page id outside the
+ *     pool, a non-finite logit) are recorded in the workspace status word and
+ *     read back with a11s_read_status(); the kernels never trap.
+ *   - A tree of N nodes is stored structure-of-arrays per sequence:
+ *     tokens[b][i], parents[b][i] with parents[b][0] == -1 (node 0 is the root,
+ *     the last token already accepted) and 0 <= parents[b][i] < i for i >= 1,
+ *     and n_nodes[b] <= max_nodes live nodes (NULL means every sequence has
+ *     max_nodes nodes). Node i's logits row is the target distribution AFTER
+ *     node i (the row used to judge node i's children and to draw a bonus).
+ *   - Logits rows are fp32 or bf16 (A11S_F32 / A11S_BF16).
+ *
+ * Reference interfaces these replace (paths inside the reference project):
+ *   engine/speculative.py:4-34                 SpeculativeDecoder (Python)
+ *   include/engine/speculative_verifier.hpp:59-125, src/engine/speculative_verifier.cpp:84-135
+ *                                              SpeculativeTreeVerifier (C++)
+ *   src/cuda/tree_verification.cu:108-210      tree_verify_kernel_launch / tree_verify (CUDA, unbound)
+ *   include/cuda/paged_kv_cache.hpp:12-67      PagedKVCacheManager block tables (16-token blocks)
+ *   engine/kv_cache.py:14-21                   KVPage layout [page_size, n_head_kv, head_dim]
+ */
+#ifndef A11SPEC_H
+#define A11SPEC_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define A11S_ABI_VERSION 1
+
+/* Status codes (return values and bits of the device status word). */
+#define A11S_OK           0
+#define A11S_EINVAL       1   /* bad host-side argument (shape, alignment, null) */
+#define A11S_EBOUNDS      2   /* device: token / page / parent id out of range */
+#define A11S_ECUDA        3   /* a CUDA runtime call failed */
+#define A11S_ETIMEOUT     4   /* device: a bounded wait gave up */
+#define A11S_ENONFINITE   5   /* device: NaN or +Inf logit (the reference throws on these,
+                                 src/engine/speculative_verifier.cpp:93-97) */
+#define A11S_ENOSPACE     6   /* workspace smaller than *_workspace_bytes() */
+#define A11S_EUNSUPPORTED 7   /* shape outside what the kernels implement */
+
+/* Element types. */
+#define A11S_F32  0
+#define A11S_BF16 1
+
+/* Acceptance modes for a11s_accept. */
+#define A11S_ACCEPT_GREEDY       0  /* accept child iff its token == argmax(parent row) */
+#define A11S_ACCEPT_STOCH_ONEHOT 1  /* rejection sampling, deterministic drafts (q = one-hot) */
+#define A11S_ACCEPT_STOCH_DRAFT  2  /* rejection sampling against draft logits q */
+
+/* Page geometry of the KV pool: 16 tokens per page, as BLOCK_TOKENS in
+ * include/cuda/paged_kv_cache.hpp:13 of the reference. */
+#define A11S_PAGE_TOKENS 16
+
+/* Diagnostic counters accumulated by a11s_accept when `stats` is non-NULL
+ * (int64 device array of A11S_STATS_LEN). The first five mirror
+ * SpecDiagnosticCounters (include/engine/speculative_verifier.hpp:31-53). */
+#define A11S_STAT_STEPS_ACCEPTED   0  /* sequences with accept_len > 0            */
+#define A11S_STAT_STEPS_REJECTED   1  /* sequences with accept_len == 0           */
+#define A11S_STAT_FALLBACKS        2  /* == STEPS_REJECTED (bonus token only)      */
+#define A11S_STAT_DRAFT_TOKENS     3  /* drafted nodes (n_nodes - 1)               */
+#define A11S_STAT_TOTAL_STEPS      4  /* sequences verified                        */
+#define A11S_STAT_EMITTED_TOKENS   5  /* accept_len + 1 (accepted + bonus)         */
+#define A11S_STATS_LEN             6
+
+int         a11s_abi_version(void);
+/* Message of the last failed call on this host thread ("" if none). */
+const char *a11s_last_error(void);
+/* Copy the workspace status word to the host. SYNCHRONISES `stream`.
+ * *status receives A11S_OK or the first device error code; *detail an index
+ * locating it (or -1). The word is cleared by the next call that uses it. */
+int a11s_read_status(const void *workspace, int32_t *status, int32_t *detail, void *stream);
+
+/* ------------------------------------------------------------------------ K3
+ * Acceptance. Replaces SpeculativeTreeVerifier::verify_draft_tokens
+ * (src/engine/speculative_verifier.cpp:84-135), SpeculativeDecoder.verify_candidates
+ * (engine/speculative.py:26-34) and tree_rejection_kernel (src/cuda/tree_verification.cu:71-101).
+ *
+ * One kernel reads every logits row once (vectorised, warp-shuffle reductions
+ * over 2048-token chunks), and the last block to finish a sequence walks its
+ * tree from the root: at each accepted node the children are tried in index
+ * order; the first accepted child becomes the next node; when none is accepted
+ * (or the node is a leaf) the bonus token is drawn at that node.
+ *
+ * GREEDY: a child is accepted iff its token == argmax of the node's row
+ *   (lowest index wins ties). bonus = argmax of the last accepted node's row.
+ * STOCH_*: p = softmax(target/T), q = softmax(draft/T) (engine/sampler.py:16),
+ *   computed by a deterministic chunked fixed-point softmax (bit-identical on
+ *   every GPU and in the CPU oracle). A child with token x and uniform u is
+ *   accepted by the reference's linear-space rule
+ *   (src/engine/speculative_verifier.cpp:114-124): ld = clamp(q(x),1e-10,1),
+ *   lt = clamp(p'(x),0,1+1e-6), accept iff u < min(1, lt/ld), where p' is the
+ *   target distribution with the residual of every rejected sibling applied:
+ *   ONEHOT drafts (q(x)=1): p' = p with the rejected tokens removed, renormalised;
+ *   DRAFT logits: p' = normalise(max(p' - q, 0)). The bonus is drawn from p'
+ *   at the final node by inverse CDF with uniforms[b][0]; uniforms[b][i] is the
+ *   acceptance uniform of node i (shape [batch][max_nodes], fp32 in [0,1)).
+ *
+ * Outputs: accept_len[b] accepted draft nodes (root excluded);
+ *   accepted_nodes[b][j], accepted_tokens[b][j] for j < accept_len (then -1),
+ *   both [batch][max_nodes]; bonus[b]; node_probs[b][i] (nullable, STOCH only)
+ *   = p(tokens[i]) in the parent's row before any residual, 0 for the root.
+ * Rows are `row_stride` elements apart (>= vocab; multiple of 8 for bf16 and
+ * of 4 for fp32; 16-byte aligned base pointers). draft_logits is used only by
+ * STOCH_DRAFT and has the same layout as target_logits.
+ */
+size_t a11s_accept_workspace_bytes(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab);
+
+int a11s_accept(int32_t mode, int32_t dtype,
+                const void *target_logits, const void *draft_logits, int64_t row_stride,
+                float temperature, const float *uniforms,
+                const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes,
+                int32_t batch, int32_t max_nodes, int32_t vocab,
+                int32_t *accept_len, int32_t *accepted_nodes, int32_t *accepted_tokens,
+                int32_t *bonus, float *node_probs, int64_t *stats,
+                void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ K2
+ * Tree-masked verification attention over the paged KV pool. Replaces the
+ * decode attention of engine/pipeline.py:386-402 (GQA by repeat_interleave,
+ * scores in fp32 scaled by `scale`, softmax, probabilities cast to bf16, PV)
+ * extended to a token tree, and tree_forward_pass_kernel
+ * (src/cuda/tree_verification.cu:34-68).
+ *
+ * q    bf16 [batch][max_nodes][num_q_heads][head_dim]
+ * k_pool, v_pool bf16 [num_pages][16][num_kv_heads][head_dim]  (engine/kv_cache.py:20-21 per page)
+ * page_table int32 [batch][max_pages_per_seq]: logical page -> physical page
+ * ctx_lens[b]: tokens before the tree. Node i's own K/V sit at logical position
+ *   ctx_lens[b] + i. Node i attends to every context position and to tree
+ *   position ctx_lens[b] + j iff j is i or an ancestor of i.
+ * out  bf16 [batch][max_nodes][num_q_heads][head_dim]; lse fp32
+ *   [batch][max_nodes][num_q_heads] natural-log sum-exp of the scaled scores
+ *   (nullable). Rows of dead nodes (i >= n_nodes[b]) are written as zeros.
+ * Implemented shapes: head_dim == 128, num_q_heads / num_kv_heads == 8,
+ * max_nodes <= 64.
+ */
+size_t a11s_tree_attention_workspace_bytes(int32_t batch, int32_t max_nodes, int32_t num_q_heads,
+                                           int32_t num_kv_heads, int32_t head_dim, int32_t max_kv_len);
+
+int a11s_tree_attention(const void *q, const void *k_pool, const void *v_pool, int32_t num_pages,
+                        const int32_t *page_table, int32_t max_pages_per_seq,
+                        const int32_t *ctx_lens, const int32_t *parents, const int32_t *n_nodes,
+                        int32_t batch, int32_t max_nodes, int32_t num_q_heads, int32_t num_kv_heads,
+                        int32_t head_dim, int32_t max_kv_len, float scale,
+                        void *out, float *lse,
+                        void *workspace, size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ K4
+ * In-place compaction of the accepted path. Replaces the host block-table
+ * bookkeeping of PagedKVCacheManager::append_token / free_sequence
+ * (src/cuda/paged_kv_cache.cu:120-158) for a verified tree.
+ *
+ * For every layer l and sequence b, the K and V rows of accepted node
+ * accepted_nodes[b][j] (logical position seq_lens[b] + node) are copied
+ * bit-for-bit to position seq_lens[b] + 1 + j, j < accept_len[b] (the root
+ * stays at seq_lens[b]). Then seq_lens[b] += 1 + accept_len[b], and every page
+ * past the new length that held tree slots (logical page index in
+ * [ceil(new_len/16), ceil((old_len + n_nodes[b])/16))) is detached:
+ * page_table[b][p] = -1 and its id appended to freed_pages[b][*], count in
+ * n_freed[b] (freed_pages / n_freed nullable).
+ * Pools: num_layers slabs `layer_stride` elements apart, each
+ * [num_pages][16][row_elems] with row_elems = num_kv_heads * head_dim,
+ * elem_bytes 2 (bf16/fp16) or 4 (fp32); row bytes must be a multiple of 16.
+ */
+int a11s_kv_compact(void *k_pool, void *v_pool, int32_t num_layers, int64_t layer_stride,
+                    int32_t num_pages, int32_t row_elems, int32_t elem_bytes,
+                    int32_t *page_table, int32_t max_pages_per_seq, int32_t *seq_lens,
+                    const int32_t *accept_len, const int32_t *accepted_nodes,
+                    const int32_t *n_nodes, int32_t batch, int32_t max_nodes,
+                    int32_t *freed_pages, int32_t *n_freed, void *workspace,
+                    size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ K1
+ * Hashed trigram drafting into a token tree. Replaces
+ * SpeculativeDecoder.generate_draft_tokens (engine/speculative.py:13-24),
+ * whose n-gram key is the last two context tokens (engine/speculative.py:21).
+ *
+ * table int32 [2^log2_buckets][slots][2] of (token, count); count <= 0 marks an
+ *   empty slot. The bucket of the token pair (a, b) is
+ *   splitmix64_finalize(((uint64)(uint32)a << 32) | (uint32)b) >> (64 - log2_buckets).
+ * last_tokens int32 [batch][2]: the two newest context tokens; node 0 (the
+ *   root) takes last_tokens[b][1].
+ * Expansion is breadth-first: a node at depth d (root d=0) gets the top
+ *   width_root (d == 0) or width_inner (d >= 1) continuations of its bucket by
+ *   count (ties: lower slot first; empty slots skipped), for d < max_depth,
+ *   until max_nodes nodes exist. Children of one parent are emitted
+ *   consecutively, parents in index order, so parents[i] < i.
+ * Outputs tokens/parents/depths [batch][max_nodes] (unused entries -1) and
+ *   n_nodes[batch].
+ */
+int a11s_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
+                      const int32_t *last_tokens, int32_t batch, int32_t width_root,
+                      int32_t width_inner, int32_t max_depth, int32_t max_nodes,
+                      int32_t *tokens, int32_t *parents, int32_t *depths, int32_t *n_nodes,
+                      void *stream);
+
+/* Bucket index the expansion uses for the pair (a, b); host-side helper so
+ * table builders agree with the device. */
+uint32_t a11s_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* A11SPEC_H */
