@@ -66,6 +66,17 @@ def accept_workspace_bytes(mode: int, batch: int, max_nodes: int, vocab: int) ->
     return int(lib.a11s_accept_workspace_bytes(mode, batch, max_nodes, vocab))
 
 
+def alloc_accept(mode: int, batch: int, max_nodes: int, vocab: int, device,
+                 want_node_probs: bool = False) -> AcceptResult:
+    """Output buffers and workspace for repeated a11s_accept calls (pass as `out`)."""
+    i32 = dict(dtype=torch.int32, device=device)
+    return AcceptResult(
+        accept_len=torch.empty(batch, **i32), accepted_nodes=torch.empty(batch, max_nodes, **i32),
+        accepted_tokens=torch.empty(batch, max_nodes, **i32), bonus=torch.empty(batch, **i32),
+        node_probs=torch.empty(batch, max_nodes, dtype=torch.float32, device=device) if want_node_probs else None,
+        workspace=workspace(accept_workspace_bytes(mode, batch, max_nodes, vocab), device))
+
+
 def accept(mode: int, target_logits: torch.Tensor, tokens: torch.Tensor, parents: torch.Tensor,
            n_nodes: Optional[torch.Tensor] = None, draft_logits: Optional[torch.Tensor] = None,
            temperature: float = 1.0, uniforms: Optional[torch.Tensor] = None,

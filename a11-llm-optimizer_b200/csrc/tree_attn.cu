@@ -1,158 +1,551 @@
-// tree_attn.cu - K2: tree-masked verification attention over 16-token KV pages.
+// tree_attn.cu - K2: tree-masked verification attention over 16-token KV pages,
+// TMA + tcgen05 (TMEM accumulators) on sm_100a.
 //
 // Math follows engine/pipeline.py:386-402 of the reference (GQA head h reads KV
-// head h / (Hq/Hkv); scores q.k * scale in fp32; softmax; probabilities in
-// bf16 for the PV product), extended to a token tree: node i sees every
-// context position and the tree positions of its ancestors and itself.
+// head h / (Hq/Hkv); scores q.k * scale in fp32; softmax; probabilities in bf16
+// for the PV product), extended to a token tree: node i sees every context
+// position and the tree positions of its ancestors and itself.
 // Semantics: include/a11spec.h (a11s_tree_attention).
+//
+// One CTA = one sequence b, one KV head g, 16 tree nodes x 8 query heads
+// (128 query rows = the MMA M), one split of the KV range. 192 threads:
+//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t)
+//   warp 4     TMA producer: Q once, then K and V blocks of 128 keys (8 pages,
+//              one 64x16 box per page and 64-column half) into a 2-stage ring
+//   warp 5     TMEM allocator + single-thread MMA issuer
+// Per block j: S_j = Q K_j^T (8 x tcgen05.mma M128 N128 K16 into TMEM, two S
+// buffers), softmax warps mask (ancestor bits), scale, exponentiate, write P_j
+// (bf16) to shared memory in the canonical 128-byte-swizzled K-major layout,
+// then O += P_j V_j (8 MMAs, V as an MN-major operand) accumulates in TMEM.
+// The running max is updated lazily: O and l are rescaled only when the block
+// max exceeds the reference max by more than 8 (log2 units), which keeps every
+// exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
+// Every mbarrier wait is bounded (clock budget); a timeout sets ETIMEOUT and
+// the CTA drains and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "tc_common.cuh"
 
 namespace a11s {
 
-constexpr int kAttnSimtWarps = 8;  // one warp per query head of a GQA group
-constexpr int kTile = 32;          // keys per tile
-constexpr int kKStride = 65;       // 32-bit words per K row in smem (64 + 1 pad)
+namespace {
+constexpr int kBlockKV = 128;
+constexpr int kNodesPerTile = 16;
+constexpr int kTcThreads = 192;
+constexpr uint32_t kHalf = 16384;    // 128 rows x 128 bytes (64 bf16 columns)
+constexpr uint32_t kTile = 32768;    // two halves
+constexpr uint32_t kOffQ = 0;
+constexpr uint32_t kOffK = kTile;            // 2 stages
+constexpr uint32_t kOffV = kOffK + 2 * kTile;
+constexpr uint32_t kOffP = kOffV + 2 * kTile;
+constexpr uint32_t kOffBar = kOffP + 2 * kTile;  // 229376
+constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
+constexpr float kRescaleThreshold = 8.0f;
+constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, 128, false);
+constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 
-int tree_attention_splits(int32_t, int32_t, int32_t, int32_t, int32_t) { return 1; }
+struct Bars {
+    uint64_t q_full;
+    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int32_t abort;
+    uint64_t anc[kNodesPerTile];
+};
+static_assert(sizeof(Bars) <= 512, "barrier block");
+
+struct TcParams {
+    const int32_t *page_table;
+    int32_t max_pages, num_pages;
+    const int32_t *ctx_lens, *parents, *n_nodes;
+    int32_t B, N, Hq, Hkv, splits;
+    float scale_log2;
+    __nv_bfloat16 *out;
+    float *lse;
+    float *part_o, *part_ml;
+    StatusWord *status;
+};
+}  // namespace
+
+int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t max_kv_len) {
+    (void)Hq;
+    int sms = 148;
+    int dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long ctas = (long long)B * Hkv * ((N + kNodesPerTile - 1) / kNodesPerTile);
+    const int blocks = (max_kv_len + kBlockKV - 1) / kBlockKV;
+    int best = 1;
+    double best_cost = 1e300;
+    for (int s = 1; s <= 16; ++s) {
+        const int bps = (blocks + s - 1) / s;
+        if (s > 1 && bps < 8) break;
+        const long long waves = (ctas * s + sms - 1) / sms;
+        const double cost = (double)waves * (bps + 4.0);  // 4 blocks of fixed per-CTA cost
+        if (cost < best_cost * 0.98) { best_cost = cost; best = s; }
+    }
+    return best;
+}
 
 size_t tree_attention_partials_bytes(int32_t B, int32_t N, int32_t Hq, int32_t D, int32_t splits) {
     return splits > 1 ? (size_t)splits * B * N * Hq * (D + 2) * sizeof(float) : 0;
 }
 
-// Ancestor-or-self bitmask of node i (bit j set iff j is i or an ancestor of i).
-__device__ __forceinline__ bool ancestors(const int32_t *par, int i, uint64_t &anc) {
-    anc = 0;
-    int a = i;
-    for (int steps = 0; steps <= 64; ++steps) {
-        anc |= 1ull << a;
-        if (a == 0) return true;
-        const int p = par[a];
-        if (p < 0 || p >= a) return false;
-        a = p;
-    }
+__device__ __forceinline__ bool aborted(Bars *bs) { return *reinterpret_cast<volatile int32_t *>(&bs->abort) != 0; }
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, Bars *bs, StatusWord *st) {
+    if (tc::mbar_wait(bar, parity, kWaitBudget)) return true;
+    *reinterpret_cast<volatile int32_t *>(&bs->abort) = 1;
+    report(st, A11S_ETIMEOUT, 0);
     return false;
 }
 
-__global__ void __launch_bounds__(kAttnSimtWarps * 32) tree_attn_simt(const AttnArgs a) {
-    const int i = blockIdx.x, g = blockIdx.y, b = blockIdx.z;
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int h = g * kAttnSimtWarps + warp;
-    const int n = a.n_nodes ? a.n_nodes[b] : a.N;
-    __nv_bfloat16 *out = reinterpret_cast<__nv_bfloat16 *>(a.out) + (((size_t)b * a.N + i) * a.Hq + h) * 128;
-    if (n < 1 || n > a.N || i >= n) {
-        if (n < 1 || n > a.N) report(a.status, A11S_EBOUNDS, b);
-        reinterpret_cast<uint2 *>(out)[lane] = make_uint2(0, 0);
-        if (a.lse && lane == 0) a.lse[((size_t)b * a.N + i) * a.Hq + h] = 0.0f;
-        return;
-    }
-    __shared__ uint64_t s_anc;
-    __shared__ int s_ok;
-    __shared__ uint32_t s_k[kTile * kKStride];
-    __shared__ uint2 s_v[kTile * 32];
-    __shared__ float s_q[kAttnSimtWarps][128];
-    __shared__ int s_valid[kTile];
-    if (threadIdx.x == 0) {
-        uint64_t anc;
-        s_ok = ancestors(a.parents + (size_t)b * a.N, i, anc);
-        s_anc = anc;
-        if (!s_ok) report(a.status, A11S_EBOUNDS, b);
-    }
-    const float qscale = a.scale * 1.4426950408889634f;  // scores in log2 units
-    {
-        const __nv_bfloat16 *qp = reinterpret_cast<const __nv_bfloat16 *>(a.q) + (((size_t)b * a.N + i) * a.Hq + h) * 128;
-        for (int d = lane; d < 128; d += 32) s_q[warp][d] = __bfloat162float(qp[d]) * qscale;
-    }
-    __syncthreads();
-    if (!s_ok) {
-        reinterpret_cast<uint2 *>(out)[lane] = make_uint2(0, 0);
-        return;
-    }
-    const int L = a.ctx_lens[b];
-    const int total = L + i + 1;
-    const uint64_t anc = s_anc;
-    const int32_t *pt = a.page_table + (size_t)b * a.max_pages;
-    const __nv_bfloat16 *kp = reinterpret_cast<const __nv_bfloat16 *>(a.k_pool);
-    const __nv_bfloat16 *vp = reinterpret_cast<const __nv_bfloat16 *>(a.v_pool);
+__global__ void __launch_bounds__(kTcThreads, 1)
+    tree_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                 const __grid_constant__ CUtensorMap tv, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars *bs = reinterpret_cast<Bars *>(sm + kOffBar);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int mt = blockIdx.x, g = blockIdx.y % p.Hkv, split = blockIdx.y / p.Hkv, b = blockIdx.z;
 
-    float m = -INFINITY, l = 0.0f;
-    float o[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int t0 = 0; t0 < total; t0 += kTile) {
-        // cooperative load of 32 K and V rows (256 B each) of KV head g
-        for (int it = threadIdx.x; it < kTile * 16; it += blockDim.x) {
-            const int t = it >> 4, c = it & 15;  // row, 16-byte column
-            const int p = t0 + t;
-            bool valid = p < total && (p < L || ((anc >> (p - L)) & 1ull));
-            int page = -1;
-            if (valid) {
-                const int lp = p / A11S_PAGE_TOKENS;
-                page = lp < a.max_pages ? pt[lp] : -1;
-                if (page < 0 || page >= a.num_pages) {
-                    report(a.status, A11S_EBOUNDS, b);
-                    valid = false;
+    int n_live = p.n_nodes ? p.n_nodes[b] : p.N;
+    if (n_live < 1 || n_live > p.N) {
+        if (tid == 0 && mt == 0 && blockIdx.y == 0) report(p.status, A11S_EBOUNDS, b);
+        n_live = 0;
+    }
+    const int node0 = mt * kNodesPerTile;
+    const int L = p.ctx_lens[b];
+    const int last_node = min(n_live, node0 + kNodesPerTile) - 1;
+    const int kv_len = L + last_node + 1;
+    const int nblk = (kv_len + kBlockKV - 1) / kBlockKV;
+    const int bps = (nblk + p.splits - 1) / p.splits;
+    const int blk0 = split * bps;
+    const int nb = last_node < node0 ? 0 : max(0, min(blk0 + bps, nblk) - blk0);
+
+    // rows of this tile: m = node_local * 8 + hh
+    const int row_node = node0 + (tid >> 3), row_head = g * 8 + (tid & 7);
+    if (nb == 0) {
+        // nothing to attend in this split (or a dead tile): empty partial / zero output
+        if (tid < 128 && row_node < p.N) {
+            const size_t row = ((size_t)b * p.N + row_node) * p.Hq + row_head;
+            if (p.splits == 1) {
+                uint4 *o = reinterpret_cast<uint4 *>(p.out + row * 128);
+                for (int c = 0; c < 16; ++c) o[c] = make_uint4(0, 0, 0, 0);
+                if (p.lse) p.lse[row] = 0.0f;
+            } else {
+                const size_t prow = ((size_t)split * p.B * p.N) * p.Hq + row;
+                p.part_ml[prow * 2] = -INFINITY;
+                p.part_ml[prow * 2 + 1] = 0.0f;
+            }
+        }
+        return;
+    }
+
+    // ---------------- setup ----------------
+    if (tid == 0) {
+        tc::mbar_init(&bs->q_full, 1);
+        for (int s = 0; s < 2; ++s) {
+            tc::mbar_init(&bs->k_full[s], 1);
+            tc::mbar_init(&bs->k_empty[s], 1);
+            tc::mbar_init(&bs->v_full[s], 1);
+            tc::mbar_init(&bs->v_empty[s], 1);
+            tc::mbar_init(&bs->s_full[s], 1);
+            tc::mbar_init(&bs->s_free[s], 128);
+            tc::mbar_init(&bs->p_full[s], 128);
+            tc::mbar_init(&bs->p_free[s], 1);
+        }
+        tc::mbar_init(&bs->drain, 1);
+        bs->abort = 0;
+        tc::fence_barrier_init();
+    }
+    if (warp == 4 && lane < kNodesPerTile) {
+        // ancestor-or-self bits of the tile's nodes
+        const int node = node0 + lane;
+        uint64_t anc = 0;
+        if (node < n_live) {
+            const int32_t *par = p.parents + (size_t)b * p.N;
+            int a = node;
+            bool ok = false;
+            for (int steps = 0; steps <= 64; ++steps) {
+                anc |= 1ull << a;
+                if (a == 0) { ok = true; break; }
+                const int pa = par[a];
+                if (pa < 0 || pa >= a) break;
+                a = pa;
+            }
+            if (!ok) {
+                report(p.status, A11S_EBOUNDS, b);
+                anc = 1ull << node;
+            }
+        }
+        bs->anc[lane] = anc;
+    }
+    if (warp == 5) {
+        tc::tmem_alloc(&bs->tmem_base, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = bs->tmem_base;
+    uint8_t *sQ = sm + kOffQ;
+
+    if (warp == 4) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&tq);
+            tc::prefetch_tmap(&tk);
+            tc::prefetch_tmap(&tv);
+            tc::mbar_arrive_expect_tx(&bs->q_full, kTile);
+            const int qrow = b * p.N + node0;
+            tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
+            tc::tma_load_3d(sQ + kHalf, &tq, &bs->q_full, 64, g * 8, qrow);
+        }
+        const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
+        for (int it = 0; it < nb && !aborted(bs); ++it) {
+            const int j = blk0 + it, s = it & 1, use = it >> 1;
+            int page = p.num_pages;  // out of range -> zero fill
+            if (lane < 8) {
+                const int lp = j * 8 + lane;
+                if (lp * A11S_PAGE_TOKENS < kv_len) {
+                    const int id = lp < p.max_pages ? pt[lp] : -1;
+                    if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
+                    else page = id;
                 }
             }
-            uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-            if (valid) {
-                const size_t row = ((size_t)page * A11S_PAGE_TOKENS + p % A11S_PAGE_TOKENS) * a.Hkv + g;
-                kv = reinterpret_cast<const uint4 *>(kp + row * 128)[c];
-                vv = reinterpret_cast<const uint4 *>(vp + row * 128)[c];
+            if (lane == 0 && use > 0) wait_or_abort(&bs->k_empty[s], (use - 1) & 1, bs, p.status);
+            __syncwarp();
+            if (aborted(bs)) break;
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->k_full[s], kTile);
+            __syncwarp();
+            uint8_t *sK = sm + kOffK + s * kTile;
+            if (lane < 8) {
+                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->k_full[s], 0, g, 0, page);
+                tc::tma_load_4d(sK + kHalf + lane * 2048, &tk, &bs->k_full[s], 64, g, 0, page);
             }
-            uint32_t *kr = s_k + t * kKStride + c * 4;
-            kr[0] = kv.x; kr[1] = kv.y; kr[2] = kv.z; kr[3] = kv.w;
-            s_v[t * 32 + c * 2] = make_uint2(vv.x, vv.y);
-            s_v[t * 32 + c * 2 + 1] = make_uint2(vv.z, vv.w);
-            if (c == 0) s_valid[t] = valid;
-        }
-        __syncthreads();
-        // score of key (t0 + lane) for this warp's head
-        float s = -INFINITY;
-        if (s_valid[lane]) {
-            const uint32_t *kr = s_k + lane * kKStride;
-            float acc = 0.f;
-#pragma unroll 8
-            for (int w = 0; w < 64; ++w) {
-                const uint32_t kw = kr[w];
-                acc = fmaf(s_q[warp][2 * w], bf16lo(kw), acc);
-                acc = fmaf(s_q[warp][2 * w + 1], bf16hi(kw), acc);
+            if (lane == 0 && use > 0) wait_or_abort(&bs->v_empty[s], (use - 1) & 1, bs, p.status);
+            __syncwarp();
+            if (aborted(bs)) break;
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->v_full[s], kTile);
+            __syncwarp();
+            uint8_t *sV = sm + kOffV + s * kTile;
+            if (lane < 8) {
+                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->v_full[s], 0, g, 0, page);
+                tc::tma_load_4d(sV + kHalf + lane * 2048, &tv, &bs->v_full[s], 64, g, 0, page);
             }
-            s = acc;
         }
-        const float mt = warp_fmax(s);
-        const float m_new = fmaxf(m, mt);
-        const float alpha = m == -INFINITY ? 0.f : exp2f(m - m_new);
-        const float p = s == -INFINITY ? 0.f : exp2f(s - m_new);
-        float ps = p;
-#pragma unroll
-        for (int off = 16; off; off >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, off);
-        l = l * alpha + ps;
-        const float pb = __bfloat162float(__float2bfloat16_rn(p));  // probabilities in bf16
-#pragma unroll
-        for (int e = 0; e < 4; ++e) o[e] *= alpha;
-        for (int t = 0; t < kTile; ++t) {
-            const float pt_ = __shfl_sync(0xffffffffu, pb, t);
-            const uint2 vw = s_v[t * 32 + lane];
-            o[0] = fmaf(pt_, bf16lo(vw.x), o[0]);
-            o[1] = fmaf(pt_, bf16hi(vw.x), o[1]);
-            o[2] = fmaf(pt_, bf16lo(vw.y), o[2]);
-            o[3] = fmaf(pt_, bf16hi(vw.y), o[3]);
+        if (aborted(bs) && lane == 0) {
+            // drain copies that may still be landing in this CTA's shared memory
+            tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
+            for (int it = max(0, nb - 2); it < nb; ++it) {
+                tc::mbar_wait(&bs->k_full[it & 1], (it >> 1) & 1, kWaitBudget);
+                tc::mbar_wait(&bs->v_full[it & 1], (it >> 1) & 1, kWaitBudget);
+            }
         }
-        m = m_new;
-        __syncthreads();
+    } else if (warp == 5) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t q_addr = tc::smem_u32(sQ);
+            auto issue_s = [&](int it) -> bool {
+                const int s = it & 1;
+                if (it >= 2 && !wait_or_abort(&bs->s_free[s], ((it >> 1) - 1) & 1, bs, p.status)) return false;
+                if (!wait_or_abort(&bs->k_full[s], (it >> 1) & 1, bs, p.status)) return false;
+                tc::tc_fence_after();
+                const uint32_t k_addr = tc::smem_u32(sm + kOffK + s * kTile);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
+                    tc::mma_bf16_ss(tmem + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
+                                    tc::sdesc_sw128(k_addr + off, 16, 1024), kIdescS, kk > 0);
+                }
+                tc::mma_commit(&bs->s_full[s]);
+                tc::mma_commit(&bs->k_empty[s]);
+                return true;
+            };
+            bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
+            ok = ok && issue_s(0);
+            for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
+                if (it + 1 < nb && !issue_s(it + 1)) break;
+                const int s = it & 1;
+                if (!wait_or_abort(&bs->p_full[s], (it >> 1) & 1, bs, p.status)) break;
+                if (!wait_or_abort(&bs->v_full[s], (it >> 1) & 1, bs, p.status)) break;
+                tc::tc_fence_after();
+                const uint32_t p_addr = tc::smem_u32(sm + kOffP + s * kTile);
+                const uint32_t v_addr = tc::smem_u32(sm + kOffV + s * kTile);
+#pragma unroll
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;
+                    tc::mma_bf16_ss(tmem + 256, tc::sdesc_sw128(p_addr + poff, 16, 1024),
+                                    tc::sdesc_sw128(v_addr + kk * 2048, kHalf, 1024), kIdescPV,
+                                    (it > 0 || kk > 0) ? 1u : 0u);
+                }
+                tc::mma_commit(&bs->p_free[s]);
+                tc::mma_commit(&bs->v_empty[s]);
+            }
+            // wait for every issued MMA before the CTA may release TMEM
+            tc::mma_commit(&bs->drain);
+            tc::mbar_wait(&bs->drain, 0, kWaitBudget);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- softmax warps 0-3 ----------------
+        const int m = tid;  // query row / TMEM lane
+        const int node_local = m >> 3;
+        const int node = node0 + node_local;
+        const bool live = node < n_live;
+        const uint64_t anc = bs->anc[node_local];
+        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        float m_ref = -INFINITY, lsum = 0.0f;
+        bool ok = true;
+        for (int it = 0; it < nb && ok; ++it) {
+            const int s = it & 1;
+            const int p0 = (blk0 + it) * kBlockKV;
+            if (!wait_or_abort(&bs->s_full[s], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+            tc::tc_fence_after();
+            float x[128];
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                float tmp[32];
+                tc::tmem_ld32(tmem + lane_base + s * 128 + c * 32, tmp);
+#pragma unroll
+                for (int e = 0; e < 32; ++e) x[c * 32 + e] = tmp[e];
+            }
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bs->s_free[s]);
+            // scale, mask, block max
+            const bool need_mask = live && (p0 + kBlockKV > L);
+            float mb = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < 128; ++c) {
+                float v = x[c] * p.scale_log2;
+                if (need_mask) {
+                    const int pos = p0 + c;
+                    const int jt = pos - L;
+                    const bool vis = pos < L || (jt <= node && ((anc >> (jt & 63)) & 1ull));
+                    v = vis ? v : -INFINITY;
+                }
+                x[c] = v;
+                mb = fmaxf(mb, v);
+            }
+            // lazy rescale of (O, l)
+            float alpha = 1.0f;
+            bool rescale = false;
+            if (mb > -INFINITY) {
+                if (m_ref == -INFINITY) {
+                    m_ref = mb;  // first visible block of this row: O row is still zero
+                } else if (mb > m_ref + kRescaleThreshold) {
+                    alpha = tc::ex2(m_ref - mb);
+                    m_ref = mb;
+                    rescale = true;
+                }
+            }
+            if (__any_sync(0xffffffffu, rescale) && it > 0) {
+                // PV(it-1) must have landed in O before it is rescaled
+                if (!wait_or_abort(&bs->p_free[(it - 1) & 1], ((it - 1) >> 1) & 1, bs, p.status)) { ok = false; break; }
+                tc::tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) o[e] *= alpha;
+                    tc::tmem_st32(tmem + lane_base + 256 + c * 32, o);
+                }
+            }
+            lsum *= alpha;
+            // P buffer s is free once PV(it-2) completed
+            if (it >= 2 && !wait_or_abort(&bs->p_free[s], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
+            const float mr = m_ref == -INFINITY ? 0.0f : m_ref;
+            uint8_t *prow = sm + kOffP + s * kTile + (m >> 3) * 1024 + (m & 7) * 128;
+#pragma unroll
+            for (int h2 = 0; h2 < 2; ++h2) {
+#pragma unroll
+                for (int c = 0; c < 8; ++c) {
+                    uint32_t w[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const int col = h2 * 64 + c * 8 + 2 * e;
+                        const float a0 = tc::ex2(x[col] - mr), a1 = tc::ex2(x[col + 1] - mr);
+                        __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+                        lsum += __low2float(pr) + __high2float(pr);
+                        w[e] = *reinterpret_cast<uint32_t *>(&pr);
+                    }
+                    *reinterpret_cast<uint4 *>(prow + h2 * kHalf + ((c ^ (m & 7)) << 4)) =
+                        make_uint4(w[0], w[1], w[2], w[3]);
+                }
+            }
+            tc::fence_proxy_async_smem();
+            tc::tc_fence_before();
+            tc::mbar_arrive(&bs->p_full[s]);
+        }
+        // ---------------- epilogue ----------------
+        if (ok && wait_or_abort(&bs->p_free[(nb - 1) & 1], ((nb - 1) >> 1) & 1, bs, p.status)) {
+            tc::tc_fence_after();
+            const size_t row = ((size_t)b * p.N + node) * p.Hq + row_head;
+            const bool write = node < p.N;
+            const float inv = lsum > 0.0f ? 1.0f / lsum : 0.0f;
+            if (p.splits == 1) {
+                uint4 *o16 = reinterpret_cast<uint4 *>(p.out + row * 128);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+                    if (write) {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q) {
+                            uint32_t w[4];
+#pragma unroll
+                            for (int e = 0; e < 4; ++e) {
+                                const float a0 = live ? o[q * 8 + 2 * e] * inv : 0.0f;
+                                const float a1 = live ? o[q * 8 + 2 * e + 1] * inv : 0.0f;
+                                __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
+                                w[e] = *reinterpret_cast<uint32_t *>(&pr);
+                            }
+                            o16[c * 4 + q] = make_uint4(w[0], w[1], w[2], w[3]);
+                        }
+                    }
+                }
+                if (write && p.lse) p.lse[row] = live && lsum > 0.0f ? (m_ref + log2f(lsum)) * 0.6931471805599453f : 0.0f;
+            } else {
+                const size_t prow = (size_t)split * p.B * p.N * p.Hq + row;
+                float4 *po = reinterpret_cast<float4 *>(p.part_o + prow * 128);
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    float o[32];
+                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+                    if (write)
+#pragma unroll
+                        for (int q = 0; q < 8; ++q)
+                            po[c * 8 + q] = make_float4(o[q * 4] * inv, o[q * 4 + 1] * inv, o[q * 4 + 2] * inv,
+                                                        o[q * 4 + 3] * inv);
+                }
+                if (write) {
+                    p.part_ml[prow * 2] = lsum > 0.0f ? m_ref : -INFINITY;
+                    p.part_ml[prow * 2 + 1] = lsum;
+                }
+            }
+        }
     }
-    const float inv = 1.0f / l;
-    __nv_bfloat162 r0 = __floats2bfloat162_rn(o[0] * inv, o[1] * inv);
-    __nv_bfloat162 r1 = __floats2bfloat162_rn(o[2] * inv, o[3] * inv);
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 5) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+}
+
+// Merge split-KV partials: one warp per (b, node, head) row.
+__global__ void tree_attn_combine(const TcParams p) {
+    const int warp_global = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    const size_t rows = (size_t)p.B * p.N * p.Hq;
+    if ((size_t)warp_global >= rows) return;
+    const size_t row = warp_global;
+    const int b = (int)(row / ((size_t)p.N * p.Hq));
+    const int node = (int)((row / p.Hq) % p.N);
+    int n_live = p.n_nodes ? p.n_nodes[b] : p.N;
+    if (n_live < 1 || n_live > p.N) n_live = 0;
+    float4 acc = make_float4(0, 0, 0, 0);
+    float M = -INFINITY, wsum = 0.0f;
+    if (node < n_live) {
+        for (int s = 0; s < p.splits; ++s) {
+            const size_t prow = (size_t)s * rows + row;
+            const float ms = p.part_ml[prow * 2], ls = p.part_ml[prow * 2 + 1];
+            if (ls > 0.0f) M = fmaxf(M, ms);
+        }
+        for (int s = 0; s < p.splits; ++s) {
+            const size_t prow = (size_t)s * rows + row;
+            const float ms = p.part_ml[prow * 2], ls = p.part_ml[prow * 2 + 1];
+            if (!(ls > 0.0f)) continue;
+            const float w = ls * exp2f(ms - M);
+            const float4 o = reinterpret_cast<const float4 *>(p.part_o + prow * 128)[lane];
+            acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
+            wsum += w;
+        }
+    }
+    const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
+    __nv_bfloat162 r0 = __floats2bfloat162_rn(acc.x * inv, acc.y * inv);
+    __nv_bfloat162 r1 = __floats2bfloat162_rn(acc.z * inv, acc.w * inv);
     uint2 packed;
     packed.x = *reinterpret_cast<uint32_t *>(&r0);
     packed.y = *reinterpret_cast<uint32_t *>(&r1);
-    reinterpret_cast<uint2 *>(out)[lane] = packed;
-    if (a.lse && lane == 0)
-        a.lse[((size_t)b * a.N + i) * a.Hq + h] = (m + log2f(l)) * 0.6931471805599453f;
+    reinterpret_cast<uint2 *>(p.out + row * 128)[lane] = packed;
+    if (p.lse && lane == 0) p.lse[row] = wsum > 0.0f ? (M + log2f(wsum)) * 0.6931471805599453f : 0.0f;
 }
 
+// ---------------------------------------------------------------------------- host side
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+bool encode(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims, const cuuint64_t *strides,
+            const cuuint32_t *box) {
+    auto fn = get_encode();
+    if (!fn) return false;
+    cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void *>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
 cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
-    tree_attn_simt<<<dim3(a.N, a.Hkv, a.B), kAttnSimtWarps * 32, 0, s>>>(a);
+    CUtensorMap tq, tk, tv;
+    {  // Q [B*N rows][Hq][128]: box 64 dims x 8 heads x 16 nodes
+        const cuuint64_t dims[3] = {128, (cuuint64_t)a.Hq, (cuuint64_t)a.B * a.N};
+        const cuuint64_t str[2] = {256, (cuuint64_t)a.Hq * 256};
+        const cuuint32_t box[3] = {64, 8, kNodesPerTile};
+        if (!encode(&tq, a.q, 3, dims, str, box)) return cudaErrorInvalidValue;
+    }
+    {  // K, V [pages][16][Hkv][128]: box 64 dims x 1 head x 16 tokens x 1 page
+        const cuuint64_t dims[4] = {128, (cuuint64_t)a.Hkv, 16, (cuuint64_t)a.num_pages};
+        const cuuint64_t str[3] = {256, (cuuint64_t)a.Hkv * 256, (cuuint64_t)a.Hkv * 256 * 16};
+        const cuuint32_t box[4] = {64, 1, 16, 1};
+        if (!encode(&tk, a.k_pool, 4, dims, str, box)) return cudaErrorInvalidValue;
+        if (!encode(&tv, a.v_pool, 4, dims, str, box)) return cudaErrorInvalidValue;
+    }
+    cudaError_t ea = cudaFuncSetAttribute(tree_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (ea != cudaSuccess) return ea;
+    TcParams p{};
+    p.page_table = a.page_table;
+    p.max_pages = a.max_pages;
+    p.num_pages = a.num_pages;
+    p.ctx_lens = a.ctx_lens;
+    p.parents = a.parents;
+    p.n_nodes = a.n_nodes;
+    p.B = a.B;
+    p.N = a.N;
+    p.Hq = a.Hq;
+    p.Hkv = a.Hkv;
+    p.splits = a.splits;
+    p.scale_log2 = a.scale * 1.4426950408889634f;
+    p.out = reinterpret_cast<__nv_bfloat16 *>(a.out);
+    p.lse = a.lse;
+    p.part_o = a.part_o;
+    p.part_ml = a.part_ml;
+    p.status = a.status;
+    const dim3 grid((a.N + kNodesPerTile - 1) / kNodesPerTile, a.Hkv * a.splits, a.B);
+    tree_attn_tc<<<grid, kTcThreads, kSmemBytes, s>>>(tq, tk, tv, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess || a.splits == 1) return e;
+    const size_t rows = (size_t)a.B * a.N * a.Hq;
+    tree_attn_combine<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, s>>>(p);
     return cudaGetLastError();
 }
 

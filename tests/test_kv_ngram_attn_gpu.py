@@ -139,9 +139,10 @@ def _attn_case(seed, B, N, Hq, Hkv, ctx, dev, ragged=True):
     return q, kv, parents, nn
 
 
-@pytest.mark.parametrize("ctx,N", [(37, 12), (300, 64), (1, 5)])
-def test_tree_attention_vs_oracle(dev, ctx, N):
-    B, Hq, Hkv = 3, 16, 2
+@pytest.mark.parametrize("ctx,N,B", [(37, 12, 3), (300, 64, 3), (1, 5, 3), (5000, 16, 1), (1000, 40, 2)])
+def test_tree_attention_vs_oracle(dev, ctx, N, B):
+    """(5000, 16, 1) and (1000, 40, 2) run with split-KV partials and the combine kernel."""
+    Hq, Hkv = 16, 2
     q, kv, parents, nn = _attn_case(7, B, N, Hq, Hkv, ctx, dev)
     out, lse, _ = a11spec.tree_attention(q, kv["k_pool"], kv["v_pool"], kv["page_table"], kv["ctx_lens"],
                                          torch.from_numpy(parents).to(dev), torch.from_numpy(nn).to(dev),
