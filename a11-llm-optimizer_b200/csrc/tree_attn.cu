@@ -10,13 +10,15 @@
 // One CTA = one sequence b, one KV head g, 16 tree nodes x 8 query heads
 // (128 query rows = the MMA M), one split of the KV range. 192 threads:
 //   warps 0-3  softmax: thread t owns query row t (= TMEM lane t)
-//   warp 4     TMA producer: Q once, then K and V blocks of 128 keys (8 pages,
-//              one 64x16 box per page and 64-column half) into a 2-stage ring
+//   warp 4     TMA producer: Q once, then K and V blocks of 64 keys (4 pages,
+//              one 64x16 box per page and 64-column half) into a 4-stage ring;
+//              page ids are fetched one block ahead
 //   warp 5     TMEM allocator + single-thread MMA issuer
-// Per block j: S_j = Q K_j^T (8 x tcgen05.mma M128 N128 K16 into TMEM, two S
-// buffers), softmax warps mask (ancestor bits), scale, exponentiate, write P_j
-// (bf16) to shared memory in the canonical 128-byte-swizzled K-major layout,
-// then O += P_j V_j (8 MMAs, V as an MN-major operand) accumulates in TMEM.
+// Per block j: S_j = Q K_j^T (8 x tcgen05.mma M128 N64 K16 into TMEM, two S
+// buffers), softmax warps mask (ancestor bits), exponentiate with one FFMA +
+// ex2 per score, pack P_j to bf16 with integer ops and write it to shared
+// memory in the canonical 128-byte-swizzled K-major layout, then
+// O += P_j V_j (4 MMAs M128 N128 K16, V as an MN-major operand) in TMEM.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
 // exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
@@ -34,25 +36,30 @@
 namespace a11s {
 
 namespace {
-constexpr int kBlockKV = 128;
+constexpr int kBlockKV = 64;          // keys per KV block = 4 pages
+constexpr int kPagesPerBlock = kBlockKV / A11S_PAGE_TOKENS;
+constexpr int kStages = 4;            // K+V ring depth
 constexpr int kNodesPerTile = 16;
 constexpr int kTcThreads = 192;
-constexpr uint32_t kHalf = 16384;    // 128 rows x 128 bytes (64 bf16 columns)
-constexpr uint32_t kTile = 32768;    // two halves
+constexpr uint32_t kQHalf = 16384;    // Q: 128 rows x 128 B per 64-dim half
+constexpr uint32_t kKVHalf = 8192;    // K or V: 64 tokens x 128 B per 64-dim half
 constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffK = kTile;            // 2 stages
-constexpr uint32_t kOffV = kOffK + 2 * kTile;
-constexpr uint32_t kOffP = kOffV + 2 * kTile;
-constexpr uint32_t kOffBar = kOffP + 2 * kTile;  // 229376
+constexpr uint32_t kOffKV = 2 * kQHalf;                      // stage s: K at +0, V at +16 KB
+constexpr uint32_t kStageBytes = 4 * kKVHalf;                // 32 KB
+constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;   // 2 buffers of 16 KB
+constexpr uint32_t kPBytes = 16384;
+constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;            // 196608
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
+constexpr uint32_t kTmemCols = 256;   // S buffers [0,64) [64,128), O [128,256)
+constexpr uint32_t kColO = 128;
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
-constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, 128, false);
+constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, kBlockKV, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 
 struct Bars {
     uint64_t q_full;
-    uint64_t k_full[2], k_empty[2], v_full[2], v_empty[2];
+    uint64_t kv_full[kStages], kv_empty[kStages];
     uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
     uint64_t drain;
     uint32_t tmem_base;
@@ -85,9 +92,9 @@ int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t
     double best_cost = 1e300;
     for (int s = 1; s <= 16; ++s) {
         const int bps = (blocks + s - 1) / s;
-        if (s > 1 && bps < 8) break;
+        if (s > 1 && bps < 16) break;
         const long long waves = (ctas * s + sms - 1) / sms;
-        const double cost = (double)waves * (bps + 4.0);  // 4 blocks of fixed per-CTA cost
+        const double cost = (double)waves * (bps + 8.0);  // ~8 blocks of fixed per-CTA cost
         if (cost < best_cost * 0.98) { best_cost = cost; best = s; }
     }
     return best;
@@ -151,11 +158,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- setup ----------------
     if (tid == 0) {
         tc::mbar_init(&bs->q_full, 1);
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(&bs->kv_full[s], 1);
+            tc::mbar_init(&bs->kv_empty[s], 1);
+        }
         for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(&bs->k_full[s], 1);
-            tc::mbar_init(&bs->k_empty[s], 1);
-            tc::mbar_init(&bs->v_full[s], 1);
-            tc::mbar_init(&bs->v_empty[s], 1);
             tc::mbar_init(&bs->s_full[s], 1);
             tc::mbar_init(&bs->s_free[s], 128);
             tc::mbar_init(&bs->p_full[s], 128);
@@ -188,7 +195,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         bs->anc[lane] = anc;
     }
     if (warp == 5) {
-        tc::tmem_alloc(&bs->tmem_base, 512);
+        tc::tmem_alloc(&bs->tmem_base, kTmemCols);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -203,91 +210,86 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc::prefetch_tmap(&tq);
             tc::prefetch_tmap(&tk);
             tc::prefetch_tmap(&tv);
-            tc::mbar_arrive_expect_tx(&bs->q_full, kTile);
+            tc::mbar_arrive_expect_tx(&bs->q_full, 2 * kQHalf);
             const int qrow = b * p.N + node0;
             tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
-            tc::tma_load_3d(sQ + kHalf, &tq, &bs->q_full, 64, g * 8, qrow);
+            tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
         }
         const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
-        for (int it = 0; it < nb && !aborted(bs); ++it) {
-            const int j = blk0 + it, s = it & 1, use = it >> 1;
-            int page = p.num_pages;  // out of range -> zero fill
-            if (lane < 8) {
-                const int lp = j * 8 + lane;
+        auto page_of = [&](int j) -> int {  // lanes 0..3: physical page of page slot `lane` of block j
+            int page = p.num_pages;         // out of range -> zero fill
+            if (lane < kPagesPerBlock && j < blk0 + nb) {
+                const int lp = j * kPagesPerBlock + lane;
                 if (lp * A11S_PAGE_TOKENS < kv_len) {
-                    const int id = lp < p.max_pages ? pt[lp] : -1;
+                    const int id = lp < p.max_pages ? __ldg(pt + lp) : -1;
                     if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
                     else page = id;
                 }
             }
-            if (lane == 0 && use > 0) wait_or_abort(&bs->k_empty[s], (use - 1) & 1, bs, p.status);
+            return page;
+        };
+        int page = page_of(blk0);
+        for (int it = 0; it < nb && !aborted(bs); ++it) {
+            const int s = it % kStages, use = it / kStages;
+            const int next_page = page_of(blk0 + it + 1);  // prefetch the next block's page ids
+            if (lane == 0 && use > 0) wait_or_abort(&bs->kv_empty[s], (use - 1) & 1, bs, p.status);
             __syncwarp();
             if (aborted(bs)) break;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->k_full[s], kTile);
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->kv_full[s], kStageBytes);
             __syncwarp();
-            uint8_t *sK = sm + kOffK + s * kTile;
-            if (lane < 8) {
-                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->k_full[s], 0, g, 0, page);
-                tc::tma_load_4d(sK + kHalf + lane * 2048, &tk, &bs->k_full[s], 64, g, 0, page);
+            uint8_t *sK = sm + kOffKV + s * kStageBytes;
+            uint8_t *sV = sK + 2 * kKVHalf;
+            if (lane < kPagesPerBlock) {
+                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->kv_full[s], 0, g, 0, page);
+                tc::tma_load_4d(sK + kKVHalf + lane * 2048, &tk, &bs->kv_full[s], 64, g, 0, page);
+                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->kv_full[s], 0, g, 0, page);
+                tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->kv_full[s], 64, g, 0, page);
             }
-            if (lane == 0 && use > 0) wait_or_abort(&bs->v_empty[s], (use - 1) & 1, bs, p.status);
-            __syncwarp();
-            if (aborted(bs)) break;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->v_full[s], kTile);
-            __syncwarp();
-            uint8_t *sV = sm + kOffV + s * kTile;
-            if (lane < 8) {
-                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->v_full[s], 0, g, 0, page);
-                tc::tma_load_4d(sV + kHalf + lane * 2048, &tv, &bs->v_full[s], 64, g, 0, page);
-            }
+            page = next_page;
         }
         if (aborted(bs) && lane == 0) {
             // drain copies that may still be landing in this CTA's shared memory
             tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
-            for (int it = max(0, nb - 2); it < nb; ++it) {
-                tc::mbar_wait(&bs->k_full[it & 1], (it >> 1) & 1, kWaitBudget);
-                tc::mbar_wait(&bs->v_full[it & 1], (it >> 1) & 1, kWaitBudget);
-            }
+            for (int it = max(0, nb - kStages); it < nb; ++it)
+                tc::mbar_wait(&bs->kv_full[it % kStages], (it / kStages) & 1, kWaitBudget);
         }
     } else if (warp == 5) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
             const uint32_t q_addr = tc::smem_u32(sQ);
             auto issue_s = [&](int it) -> bool {
-                const int s = it & 1;
-                if (it >= 2 && !wait_or_abort(&bs->s_free[s], ((it >> 1) - 1) & 1, bs, p.status)) return false;
-                if (!wait_or_abort(&bs->k_full[s], (it >> 1) & 1, bs, p.status)) return false;
+                const int sb = it & 1, st = it % kStages;
+                if (it >= 2 && !wait_or_abort(&bs->s_free[sb], ((it >> 1) - 1) & 1, bs, p.status)) return false;
+                if (!wait_or_abort(&bs->kv_full[st], (it / kStages) & 1, bs, p.status)) return false;
                 tc::tc_fence_after();
-                const uint32_t k_addr = tc::smem_u32(sm + kOffK + s * kTile);
+                const uint32_t k_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t off = (kk >> 2) * kHalf + (kk & 3) * 32;
-                    tc::mma_bf16_ss(tmem + s * 128, tc::sdesc_sw128(q_addr + off, 16, 1024),
-                                    tc::sdesc_sw128(k_addr + off, 16, 1024), kIdescS, kk > 0);
+                    const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+                    const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+                    tc::mma_bf16_ss(tmem + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
+                                    tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
                 }
-                tc::mma_commit(&bs->s_full[s]);
-                tc::mma_commit(&bs->k_empty[s]);
+                tc::mma_commit(&bs->s_full[sb]);
                 return true;
             };
             bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
             ok = ok && issue_s(0);
             for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
                 if (it + 1 < nb && !issue_s(it + 1)) break;
-                const int s = it & 1;
-                if (!wait_or_abort(&bs->p_full[s], (it >> 1) & 1, bs, p.status)) break;
-                if (!wait_or_abort(&bs->v_full[s], (it >> 1) & 1, bs, p.status)) break;
+                const int pb = it & 1, st = it % kStages;
+                if (!wait_or_abort(&bs->p_full[pb], (it >> 1) & 1, bs, p.status)) break;
                 tc::tc_fence_after();
-                const uint32_t p_addr = tc::smem_u32(sm + kOffP + s * kTile);
-                const uint32_t v_addr = tc::smem_u32(sm + kOffV + s * kTile);
+                const uint32_t p_addr = tc::smem_u32(sm + kOffP + pb * kPBytes);
+                const uint32_t v_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes + 2 * kKVHalf);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t poff = (kk >> 2) * kHalf + (kk & 3) * 32;
-                    tc::mma_bf16_ss(tmem + 256, tc::sdesc_sw128(p_addr + poff, 16, 1024),
-                                    tc::sdesc_sw128(v_addr + kk * 2048, kHalf, 1024), kIdescPV,
+                for (int kk = 0; kk < kBlockKV / 16; ++kk) {
+                    tc::mma_bf16_ss(tmem + kColO, tc::sdesc_sw128(p_addr + kk * 32, 16, 1024),
+                                    tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
                                     (it > 0 || kk > 0) ? 1u : 0u);
                 }
-                tc::mma_commit(&bs->p_free[s]);
-                tc::mma_commit(&bs->v_empty[s]);
+                tc::mma_commit(&bs->p_free[pb]);
+                tc::mma_commit(&bs->kv_empty[st]);
             }
             // wait for every issued MMA before the CTA may release TMEM
             tc::mma_commit(&bs->drain);
@@ -302,44 +304,43 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         const bool live = node < n_live;
         const uint64_t anc = bs->anc[node_local];
         const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const float sl2 = p.scale_log2;
         float m_ref = -INFINITY, lsum = 0.0f;
         bool ok = true;
         for (int it = 0; it < nb && ok; ++it) {
-            const int s = it & 1;
+            const int sb = it & 1;
             const int p0 = (blk0 + it) * kBlockKV;
-            if (!wait_or_abort(&bs->s_full[s], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+            if (!wait_or_abort(&bs->s_full[sb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
             tc::tc_fence_after();
-            float x[128];
+            float x[kBlockKV];
+            {
+                float t0[32], t1[32];
+                tc::tmem_ld32(tmem + lane_base + sb * kBlockKV, t0);
+                tc::tmem_ld32(tmem + lane_base + sb * kBlockKV + 32, t1);
 #pragma unroll
-            for (int c = 0; c < 4; ++c) {
-                float tmp[32];
-                tc::tmem_ld32(tmem + lane_base + s * 128 + c * 32, tmp);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) x[c * 32 + e] = tmp[e];
+                for (int e = 0; e < 32; ++e) { x[e] = t0[e]; x[32 + e] = t1[e]; }
             }
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->s_free[s]);
-            // scale, mask, block max
-            const bool need_mask = live && (p0 + kBlockKV > L);
-            float mb = -INFINITY;
+            tc::mbar_arrive(&bs->s_free[sb]);
+            // mask (raw scores) and block max
+            if (live && p0 + kBlockKV > L) {
 #pragma unroll
-            for (int c = 0; c < 128; ++c) {
-                float v = x[c] * p.scale_log2;
-                if (need_mask) {
-                    const int pos = p0 + c;
-                    const int jt = pos - L;
-                    const bool vis = pos < L || (jt <= node && ((anc >> (jt & 63)) & 1ull));
-                    v = vis ? v : -INFINITY;
+                for (int c = 0; c < kBlockKV; ++c) {
+                    const int jt = p0 + c - L;
+                    const bool vis = jt < 0 || (jt <= node && ((anc >> (jt & 63)) & 1ull));
+                    x[c] = vis ? x[c] : -INFINITY;
                 }
-                x[c] = v;
-                mb = fmaxf(mb, v);
             }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < kBlockKV; ++c) mx = fmaxf(mx, x[c]);
+            const float mb = mx * sl2;  // scale > 0: max commutes with scaling
             // lazy rescale of (O, l)
             float alpha = 1.0f;
             bool rescale = false;
-            if (mb > -INFINITY) {
+            if (mx > -INFINITY) {
                 if (m_ref == -INFINITY) {
-                    m_ref = mb;  // first visible block of this row: O row is still zero
+                    m_ref = mb;  // first visible block of this row: its O row is still zero
                 } else if (mb > m_ref + kRescaleThreshold) {
                     alpha = tc::ex2(m_ref - mb);
                     m_ref = mb;
@@ -353,37 +354,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                    tc::tmem_st32(tmem + lane_base + 256 + c * 32, o);
+                    tc::tmem_st32(tmem + lane_base + kColO + c * 32, o);
                 }
             }
             lsum *= alpha;
-            // P buffer s is free once PV(it-2) completed
-            if (it >= 2 && !wait_or_abort(&bs->p_free[s], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
-            const float mr = m_ref == -INFINITY ? 0.0f : m_ref;
-            uint8_t *prow = sm + kOffP + s * kTile + (m >> 3) * 1024 + (m & 7) * 128;
+            // P buffer sb is free once PV(it-2) completed
+            if (it >= 2 && !wait_or_abort(&bs->p_free[sb], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
+            const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
+            uint8_t *prow = sm + kOffP + sb * kPBytes + (m >> 3) * 1024 + (m & 7) * 128;
 #pragma unroll
-            for (int h2 = 0; h2 < 2; ++h2) {
+            for (int c = 0; c < 8; ++c) {
+                uint32_t w[4];
 #pragma unroll
-                for (int c = 0; c < 8; ++c) {
-                    uint32_t w[4];
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int col = h2 * 64 + c * 8 + 2 * e;
-                        const float a0 = tc::ex2(x[col] - mr), a1 = tc::ex2(x[col + 1] - mr);
-                        __nv_bfloat162 pr = __floats2bfloat162_rn(a0, a1);
-                        lsum += __low2float(pr) + __high2float(pr);
-                        w[e] = *reinterpret_cast<uint32_t *>(&pr);
-                    }
-                    *reinterpret_cast<uint4 *>(prow + h2 * kHalf + ((c ^ (m & 7)) << 4)) =
-                        make_uint4(w[0], w[1], w[2], w[3]);
+                for (int e = 0; e < 4; ++e) {
+                    const int col = c * 8 + 2 * e;
+                    const float a0 = tc::ex2(fmaf(x[col], sl2, neg));
+                    const float a1 = tc::ex2(fmaf(x[col + 1], sl2, neg));
+                    lsum += a0 + a1;
+                    // bf16 by rounding half up on the bit pattern (a >= 0, finite)
+                    w[e] = __byte_perm(__float_as_uint(a0) + 0x8000u, __float_as_uint(a1) + 0x8000u, 0x7632);
                 }
+                *reinterpret_cast<uint4 *>(prow + ((c ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
             tc::fence_proxy_async_smem();
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->p_full[s]);
+            tc::mbar_arrive(&bs->p_full[sb]);
         }
         // ---------------- epilogue ----------------
         if (ok && wait_or_abort(&bs->p_free[(nb - 1) & 1], ((nb - 1) >> 1) & 1, bs, p.status)) {
@@ -396,7 +394,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
                     if (write) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
@@ -419,7 +417,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + 256 + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
                     if (write)
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
@@ -437,7 +435,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     if (warp == 5) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 512);
+        tc::tmem_dealloc(tmem, kTmemCols);
     }
 }
 
