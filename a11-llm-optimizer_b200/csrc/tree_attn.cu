@@ -7,17 +7,18 @@
 // position and the tree positions of its ancestors and itself.
 // Semantics: include/a11spec.h (a11s_tree_attention).
 //
-// One CTA = one sequence b, one KV head g, 16 tree nodes x 8 query heads
-// (128 query rows = the MMA M), one split of the KV range. 192 threads:
-//   warps 0-3  softmax: thread t owns query row t (= TMEM lane t)
-//   warp 4     TMA producer: Q once, then K and V blocks of 64 keys (4 pages,
-//              one 64x16 box per page and 64-column half) into a 4-stage ring;
-//              page ids are fetched one block ahead
-//   warp 5     TMEM allocator + single-thread MMA issuer
-// Per block j: S_j = Q K_j^T (8 x tcgen05.mma M128 N64 K16 into TMEM, two S
-// buffers), softmax warps mask (ancestor bits), exponentiate with one FFMA +
-// ex2 per score, pack P_j to bf16 with integer ops and write it to shared
-// memory in the canonical 128-byte-swizzled K-major layout, then
+// One CTA = one sequence b, one KV head g, 32 tree nodes x 8 query heads as
+// two Q tiles of 128 rows (the MMA M), one split of the KV range. 320 threads:
+//   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane;
+//              two softmax warps per scheduler hide each other's latency
+//   warp 8     TMA producer: Q once, then K and V blocks of 64 keys (4 pages,
+//              one 64x16 box per page and 64-column half) into a 3-stage ring
+//              shared by both tiles; page ids fetched 8 blocks ahead
+//   warp 9     TMEM allocator + single-thread MMA issuer
+// Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N64 K16 into TMEM,
+// two S buffers per tile), softmax warps mask (ancestor bits), exponentiate
+// with one FFMA + ex2 per score, pack P_j to bf16 with integer ops and write
+// it to shared memory in the canonical 128-byte-swizzled K-major layout, then
 // O += P_j V_j (4 MMAs M128 N128 K16, V as an MN-major operand) in TMEM.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
@@ -38,20 +39,24 @@ namespace a11s {
 namespace {
 constexpr int kBlockKV = 64;          // keys per KV block = 4 pages
 constexpr int kPagesPerBlock = kBlockKV / A11S_PAGE_TOKENS;
-constexpr int kStages = 4;            // K+V ring depth
+constexpr int kStages = 3;            // K+V ring depth (each stage serves both Q tiles)
+constexpr int kTiles = 2;             // Q tiles per CTA, 128 rows each
 constexpr int kNodesPerTile = 16;
-constexpr int kTcThreads = 192;
-constexpr uint32_t kQHalf = 16384;    // Q: 128 rows x 128 B per 64-dim half
+constexpr int kNodesPerCta = kTiles * kNodesPerTile;
+constexpr int kSoftmaxWarps = 4 * kTiles;
+constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
+constexpr int kTcThreads = 32 * (kSoftmaxWarps + 2);
+constexpr uint32_t kQHalf = 16384;    // Q tile: 128 rows x 128 B per 64-dim half
 constexpr uint32_t kKVHalf = 8192;    // K or V: 64 tokens x 128 B per 64-dim half
-constexpr uint32_t kOffQ = 0;
-constexpr uint32_t kOffKV = 2 * kQHalf;                      // stage s: K at +0, V at +16 KB
+constexpr uint32_t kOffQ = 0;                                // tile t at 2*kQHalf*t
+constexpr uint32_t kOffKV = kTiles * 2 * kQHalf;             // stage s: K at +0, V at +16 KB
 constexpr uint32_t kStageBytes = 4 * kKVHalf;                // 32 KB
-constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;   // 2 buffers of 16 KB
+constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;   // [tile][buffer] x 16 KB
 constexpr uint32_t kPBytes = 16384;
-constexpr uint32_t kOffBar = kOffP + 2 * kPBytes;            // 196608
+constexpr uint32_t kOffBar = kOffP + kTiles * 2 * kPBytes;   // 229376
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-constexpr uint32_t kTmemCols = 256;   // S buffers [0,64) [64,128), O [128,256)
-constexpr uint32_t kColO = 128;
+constexpr uint32_t kTmemCols = 512;   // S [tile][buffer] at 128 t + 64 b, O[tile] at 256 + 128 t
+constexpr uint32_t kColO = 256;
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, kBlockKV, false);
@@ -60,13 +65,14 @@ constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[kStages], kv_empty[kStages];
-    uint64_t s_full[2], s_free[2], p_full[2], p_free[2];
+    uint64_t s_full[kTiles][2], s_free[kTiles][2], p_full[kTiles][2], p_free[kTiles][2];
     uint64_t drain;
     uint32_t tmem_base;
     int32_t abort;
-    uint64_t anc[kNodesPerTile];
+    uint64_t anc[kNodesPerCta];
 };
 static_assert(sizeof(Bars) <= 512, "barrier block");
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct TcParams {
     const int32_t *page_table;
@@ -86,11 +92,11 @@ int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t
     int sms = 148;
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long ctas = (long long)B * Hkv * ((N + kNodesPerTile - 1) / kNodesPerTile);
+    const long long ctas = (long long)B * Hkv * ((N + kNodesPerCta - 1) / kNodesPerCta);
     const int blocks = (max_kv_len + kBlockKV - 1) / kBlockKV;
     int best = 1;
     double best_cost = 1e300;
-    for (int s = 1; s <= 16; ++s) {
+    for (int s = 1; s <= 32; ++s) {
         const int bps = (blocks + s - 1) / s;
         if (s > 1 && bps < 16) break;
         const long long waves = (ctas * s + sms - 1) / sms;
@@ -113,6 +119,12 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, Ba
     return false;
 }
 
+// bf16 pair by rounding half up on the bit patterns (a >= 0 and finite here):
+// unbiased to within the half-way ties, two integer adds and one byte permute.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a0, float a1) {
+    return __byte_perm(__float_as_uint(a0) + 0x8000u, __float_as_uint(a1) + 0x8000u, 0x7632);
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     tree_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const TcParams p) {
@@ -120,28 +132,30 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars *bs = reinterpret_cast<Bars *>(sm + kOffBar);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int mt = blockIdx.x, g = blockIdx.y % p.Hkv, split = blockIdx.y / p.Hkv, b = blockIdx.z;
+    const int ct = blockIdx.x, g = blockIdx.y % p.Hkv, split = blockIdx.y / p.Hkv, b = blockIdx.z;
 
     int n_live = p.n_nodes ? p.n_nodes[b] : p.N;
     if (n_live < 1 || n_live > p.N) {
-        if (tid == 0 && mt == 0 && blockIdx.y == 0) report(p.status, A11S_EBOUNDS, b);
+        if (tid == 0 && ct == 0 && blockIdx.y == 0) report(p.status, A11S_EBOUNDS, b);
         n_live = 0;
     }
-    const int node0 = mt * kNodesPerTile;
+    const int node0 = ct * kNodesPerCta;
     const int L = p.ctx_lens[b];
-    const int last_node = min(n_live, node0 + kNodesPerTile) - 1;
+    const int last_node = min(n_live, node0 + kNodesPerCta) - 1;
     const int kv_len = L + last_node + 1;
     const int nblk = (kv_len + kBlockKV - 1) / kBlockKV;
     const int bps = (nblk + p.splits - 1) / p.splits;
     const int blk0 = split * bps;
     const int nb = last_node < node0 ? 0 : max(0, min(blk0 + bps, nblk) - blk0);
 
-    // rows of this tile: m = node_local * 8 + hh
-    const int row_node = node0 + (tid >> 3), row_head = g * 8 + (tid & 7);
+    // softmax thread -> (tile, query row m = node_local * 8 + hh)
+    const int tile = warp / 4 < kTiles ? warp / 4 : 0;
+    const int m = tid & 127;
+    const int node = node0 + tile * kNodesPerTile + (m >> 3), row_head = g * 8 + (m & 7);
     if (nb == 0) {
-        // nothing to attend in this split (or a dead tile): empty partial / zero output
-        if (tid < 128 && row_node < p.N) {
-            const size_t row = ((size_t)b * p.N + row_node) * p.Hq + row_head;
+        // nothing to attend in this split (or a dead CTA): empty partial / zero output
+        if (warp < kSoftmaxWarps && node < p.N) {
+            const size_t row = ((size_t)b * p.N + node) * p.Hq + row_head;
             if (p.splits == 1) {
                 uint4 *o = reinterpret_cast<uint4 *>(p.out + row * 128);
                 for (int c = 0; c < 16; ++c) o[c] = make_uint4(0, 0, 0, 0);
@@ -162,23 +176,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc::mbar_init(&bs->kv_full[s], 1);
             tc::mbar_init(&bs->kv_empty[s], 1);
         }
-        for (int s = 0; s < 2; ++s) {
-            tc::mbar_init(&bs->s_full[s], 1);
-            tc::mbar_init(&bs->s_free[s], 128);
-            tc::mbar_init(&bs->p_full[s], 128);
-            tc::mbar_init(&bs->p_free[s], 1);
-        }
+        for (int t = 0; t < kTiles; ++t)
+            for (int s = 0; s < 2; ++s) {
+                tc::mbar_init(&bs->s_full[t][s], 1);
+                tc::mbar_init(&bs->s_free[t][s], 128);
+                tc::mbar_init(&bs->p_full[t][s], 128);
+                tc::mbar_init(&bs->p_free[t][s], 1);
+            }
         tc::mbar_init(&bs->drain, 1);
         bs->abort = 0;
         tc::fence_barrier_init();
     }
-    if (warp == 4 && lane < kNodesPerTile) {
-        // ancestor-or-self bits of the tile's nodes
-        const int node = node0 + lane;
+    if (warp == kProducerWarp) {
+        // ancestor-or-self bits of the CTA's nodes (lane = node offset)
+        const int nd = node0 + lane;
         uint64_t anc = 0;
-        if (node < n_live) {
+        if (nd < n_live) {
             const int32_t *par = p.parents + (size_t)b * p.N;
-            int a = node;
+            int a = nd;
             bool ok = false;
             for (int steps = 0; steps <= 64; ++steps) {
                 anc |= 1ull << a;
@@ -189,12 +204,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (!ok) {
                 report(p.status, A11S_EBOUNDS, b);
-                anc = 1ull << node;
+                anc = 1ull << nd;
             }
         }
         bs->anc[lane] = anc;
     }
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc::tmem_alloc(&bs->tmem_base, kTmemCols);
         tc::tmem_relinquish();
     }
@@ -202,36 +217,44 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = bs->tmem_base;
-    uint8_t *sQ = sm + kOffQ;
 
-    if (warp == 4) {
+    if (warp == kProducerWarp) {
         // ---------------- TMA producer ----------------
         if (lane == 0) {
             tc::prefetch_tmap(&tq);
             tc::prefetch_tmap(&tk);
             tc::prefetch_tmap(&tv);
-            tc::mbar_arrive_expect_tx(&bs->q_full, 2 * kQHalf);
-            const int qrow = b * p.N + node0;
-            tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
-            tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
-        }
-        const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
-        auto page_of = [&](int j) -> int {  // lanes 0..3: physical page of page slot `lane` of block j
-            int page = p.num_pages;         // out of range -> zero fill
-            if (lane < kPagesPerBlock && j < blk0 + nb) {
-                const int lp = j * kPagesPerBlock + lane;
-                if (lp * A11S_PAGE_TOKENS < kv_len) {
-                    const int id = lp < p.max_pages ? __ldg(pt + lp) : -1;
-                    if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
-                    else page = id;
-                }
+            tc::mbar_arrive_expect_tx(&bs->q_full, kTiles * 2 * kQHalf);
+            for (int t = 0; t < kTiles; ++t) {
+                const int qrow = b * p.N + node0 + t * kNodesPerTile;
+                uint8_t *sQ = sm + kOffQ + t * 2 * kQHalf;
+                tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
+                tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
             }
-            return page;
+        }
+        // Page ids of 8 blocks (32 entries) per coalesced warp load, double
+        // buffered, so a block's ids were requested 8 blocks before use.
+        const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
+        const int lp0 = blk0 * kPagesPerBlock;
+        const int lp_end = min((kv_len + A11S_PAGE_TOKENS - 1) / A11S_PAGE_TOKENS, (blk0 + nb) * kPagesPerBlock);
+        auto window = [&](int w) -> int {  // entry lp0 + 32 w + lane, or -2 past the needed range
+            const int lp = lp0 + 32 * w + lane;
+            if (lp >= lp_end) return -2;
+            return lp < p.max_pages ? __ldg(pt + lp) : -1;
         };
-        int page = page_of(blk0);
+        int cur = window(0), nxt = window(1);
         for (int it = 0; it < nb && !aborted(bs); ++it) {
-            const int s = it % kStages, use = it / kStages;
-            const int next_page = page_of(blk0 + it + 1);  // prefetch the next block's page ids
+            const int s = it % kStages, use = it / kStages, k = it & 7;
+            if (k == 0 && it > 0) {
+                cur = nxt;
+                nxt = window((it >> 3) + 1);
+            }
+            const int id = __shfl_sync(0xffffffffu, cur, (k * kPagesPerBlock + lane) & 31);
+            int page = p.num_pages;  // out of range -> zero fill
+            if (lane < kPagesPerBlock && id != -2) {
+                if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
+                else page = id;
+            }
             if (lane == 0 && use > 0) wait_or_abort(&bs->kv_empty[s], (use - 1) & 1, bs, p.status);
             __syncwarp();
             if (aborted(bs)) break;
@@ -245,7 +268,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc::tma_load_4d(sV + lane * 2048, &tv, &bs->kv_full[s], 0, g, 0, page);
                 tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->kv_full[s], 64, g, 0, page);
             }
-            page = next_page;
         }
         if (aborted(bs) && lane == 0) {
             // drain copies that may still be landing in this CTA's shared memory
@@ -253,24 +275,26 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int it = max(0, nb - kStages); it < nb; ++it)
                 tc::mbar_wait(&bs->kv_full[it % kStages], (it / kStages) & 1, kWaitBudget);
         }
-    } else if (warp == 5) {
+    } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            const uint32_t q_addr = tc::smem_u32(sQ);
             auto issue_s = [&](int it) -> bool {
                 const int sb = it & 1, st = it % kStages;
-                if (it >= 2 && !wait_or_abort(&bs->s_free[sb], ((it >> 1) - 1) & 1, bs, p.status)) return false;
                 if (!wait_or_abort(&bs->kv_full[st], (it / kStages) & 1, bs, p.status)) return false;
-                tc::tc_fence_after();
                 const uint32_t k_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes);
+                for (int t = 0; t < kTiles; ++t) {
+                    if (it >= 2 && !wait_or_abort(&bs->s_free[t][sb], ((it >> 1) - 1) & 1, bs, p.status)) return false;
+                    tc::tc_fence_after();
+                    const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
 #pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-                    const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                    tc::mma_bf16_ss(tmem + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
-                                    tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+                        const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+                        tc::mma_bf16_ss(tmem + t * 128 + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
+                                        tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
+                    }
+                    tc::mma_commit(&bs->s_full[t][sb]);
                 }
-                tc::mma_commit(&bs->s_full[sb]);
                 return true;
             };
             bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
@@ -278,17 +302,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
                 if (it + 1 < nb && !issue_s(it + 1)) break;
                 const int pb = it & 1, st = it % kStages;
-                if (!wait_or_abort(&bs->p_full[pb], (it >> 1) & 1, bs, p.status)) break;
-                tc::tc_fence_after();
-                const uint32_t p_addr = tc::smem_u32(sm + kOffP + pb * kPBytes);
                 const uint32_t v_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes + 2 * kKVHalf);
+                for (int t = 0; t < kTiles && ok; ++t) {
+                    if (!wait_or_abort(&bs->p_full[t][pb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+                    tc::tc_fence_after();
+                    const uint32_t p_addr = tc::smem_u32(sm + kOffP + (t * 2 + pb) * kPBytes);
 #pragma unroll
-                for (int kk = 0; kk < kBlockKV / 16; ++kk) {
-                    tc::mma_bf16_ss(tmem + kColO, tc::sdesc_sw128(p_addr + kk * 32, 16, 1024),
-                                    tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
-                                    (it > 0 || kk > 0) ? 1u : 0u);
+                    for (int kk = 0; kk < kBlockKV / 16; ++kk) {
+                        tc::mma_bf16_ss(tmem + kColO + t * 128, tc::sdesc_sw128(p_addr + kk * 32, 16, 1024),
+                                        tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
+                                        (it > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    tc::mma_commit(&bs->p_free[t][pb]);
                 }
-                tc::mma_commit(&bs->p_free[pb]);
                 tc::mma_commit(&bs->kv_empty[st]);
             }
             // wait for every issued MMA before the CTA may release TMEM
@@ -297,31 +323,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         __syncwarp();
     } else {
-        // ---------------- softmax warps 0-3 ----------------
-        const int m = tid;  // query row / TMEM lane
-        const int node_local = m >> 3;
-        const int node = node0 + node_local;
+        // ---------------- softmax warps: tile = warp / 4, thread = query row ----------------
         const bool live = node < n_live;
-        const uint64_t anc = bs->anc[node_local];
-        const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+        const uint64_t anc = bs->anc[node - node0];
+        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t col_s = tile * 128, col_o = kColO + tile * 128;
         const float sl2 = p.scale_log2;
         float m_ref = -INFINITY, lsum = 0.0f;
         bool ok = true;
         for (int it = 0; it < nb && ok; ++it) {
             const int sb = it & 1;
             const int p0 = (blk0 + it) * kBlockKV;
-            if (!wait_or_abort(&bs->s_full[sb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+            if (!wait_or_abort(&bs->s_full[tile][sb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
             tc::tc_fence_after();
             float x[kBlockKV];
-            {
-                float t0[32], t1[32];
-                tc::tmem_ld32(tmem + lane_base + sb * kBlockKV, t0);
-                tc::tmem_ld32(tmem + lane_base + sb * kBlockKV + 32, t1);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) { x[e] = t0[e]; x[32 + e] = t1[e]; }
-            }
+            tc::tmem_ld64(tmem + lane_base + col_s + sb * kBlockKV, x);
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->s_free[sb]);
+            tc::mbar_arrive(&bs->s_free[tile][sb]);
             // mask (raw scores) and block max
             if (live && p0 + kBlockKV > L) {
 #pragma unroll
@@ -331,9 +349,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     x[c] = vis ? x[c] : -INFINITY;
                 }
             }
-            float mx = -INFINITY;
+            float mx8[8];  // 8 independent chains, then a tree
 #pragma unroll
-            for (int c = 0; c < kBlockKV; ++c) mx = fmaxf(mx, x[c]);
+            for (int q = 0; q < 8; ++q) mx8[q] = x[q];
+#pragma unroll
+            for (int c = 8; c < kBlockKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
+            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float mb = mx * sl2;  // scale > 0: max commutes with scaling
             // lazy rescale of (O, l)
             float alpha = 1.0f;
@@ -349,22 +371,23 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (__any_sync(0xffffffffu, rescale) && it > 0) {
                 // PV(it-1) must have landed in O before it is rescaled
-                if (!wait_or_abort(&bs->p_free[(it - 1) & 1], ((it - 1) >> 1) & 1, bs, p.status)) { ok = false; break; }
+                if (!wait_or_abort(&bs->p_free[tile][(it - 1) & 1], ((it - 1) >> 1) & 1, bs, p.status)) { ok = false; break; }
                 tc::tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                    tc::tmem_st32(tmem + lane_base + kColO + c * 32, o);
+                    tc::tmem_st32(tmem + lane_base + col_o + c * 32, o);
                 }
             }
             lsum *= alpha;
             // P buffer sb is free once PV(it-2) completed
-            if (it >= 2 && !wait_or_abort(&bs->p_free[sb], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
+            if (it >= 2 && !wait_or_abort(&bs->p_free[tile][sb], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
             const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
-            uint8_t *prow = sm + kOffP + sb * kPBytes + (m >> 3) * 1024 + (m & 7) * 128;
+            uint8_t *prow = sm + kOffP + (tile * 2 + sb) * kPBytes + (m >> 3) * 1024 + (m & 7) * 128;
+            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
             for (int c = 0; c < 8; ++c) {
                 uint32_t w[4];
@@ -373,18 +396,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const int col = c * 8 + 2 * e;
                     const float a0 = tc::ex2(fmaf(x[col], sl2, neg));
                     const float a1 = tc::ex2(fmaf(x[col + 1], sl2, neg));
-                    lsum += a0 + a1;
-                    // bf16 by rounding half up on the bit pattern (a >= 0, finite)
-                    w[e] = __byte_perm(__float_as_uint(a0) + 0x8000u, __float_as_uint(a1) + 0x8000u, 0x7632);
+                    w[e] = pack_bf16x2(a0, a1);
+                    // the row sum uses the bf16 values the PV product sees
+                    ls[(2 * e) & 7] += __uint_as_float(w[e] << 16);
+                    ls[(2 * e + 1) & 7] += __uint_as_float(w[e] & 0xFFFF0000u);
                 }
                 *reinterpret_cast<uint4 *>(prow + ((c ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }
+            lsum += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
             tc::fence_proxy_async_smem();
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->p_full[sb]);
+            tc::mbar_arrive(&bs->p_full[tile][sb]);
         }
         // ---------------- epilogue ----------------
-        if (ok && wait_or_abort(&bs->p_free[(nb - 1) & 1], ((nb - 1) >> 1) & 1, bs, p.status)) {
+        if (ok && wait_or_abort(&bs->p_free[tile][(nb - 1) & 1], ((nb - 1) >> 1) & 1, bs, p.status)) {
             tc::tc_fence_after();
             const size_t row = ((size_t)b * p.N + node) * p.Hq + row_head;
             const bool write = node < p.N;
@@ -394,7 +419,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
                     if (write) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
@@ -417,7 +442,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + kColO + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
                     if (write)
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
@@ -433,7 +458,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (warp == 5) {
+    if (warp == kMmaWarp) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, kTmemCols);
     }
@@ -538,7 +563,7 @@ cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
     p.part_o = a.part_o;
     p.part_ml = a.part_ml;
     p.status = a.status;
-    const dim3 grid((a.N + kNodesPerTile - 1) / kNodesPerTile, a.Hkv * a.splits, a.B);
+    const dim3 grid((a.N + kNodesPerCta - 1) / kNodesPerCta, a.Hkv * a.splits, a.B);
     tree_attn_tc<<<grid, kTcThreads, kSmemBytes, s>>>(tq, tk, tv, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || a.splits == 1) return e;
