@@ -63,6 +63,10 @@ AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32
 
 }  // namespace
 
+namespace a11s {
+int set_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace a11s
+
 extern "C" {
 
 int a11s_abi_version(void) { return A11S_ABI_VERSION; }

@@ -92,6 +92,9 @@ struct AttnArgs {
 };
 
 cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s);
+
+// Records `msg` as this thread's a11s_last_error() and returns `code`.
+int set_error(int code, const char *msg);
 size_t tree_attention_partials_bytes(int32_t B, int32_t N, int32_t Hq, int32_t D, int32_t splits);
 int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t max_kv_len);
 

@@ -135,6 +135,31 @@ int a11s_accept(int32_t mode, int32_t dtype,
                 int32_t *bonus, float *node_probs, int64_t *stats,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/* Fixed-scratch variant of a11s_accept, with no counterpart in the reference.
+ * For callers that cannot pass a workspace because they may not allocate
+ * device memory: hosts whose HBM is owned by another allocator that forbids
+ * outside cudaMalloc calls, foreign-language bindings without a device
+ * allocator, decode loops that cannot afford cudaMalloc's possible device-wide
+ * synchronisation. The scratch is one file-scope device array of
+ * A11S_ACCEPT_STATIC_SCRATCH_BYTES (4 MiB) that every GPU loading the library
+ * holds until the process exits; calls whose a11s_accept_workspace_bytes()
+ * exceeds it return A11S_ENOSPACE. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress); make that first call before
+ * any stream capture. All calls share the array: calls that overlap on the GPU
+ * (other streams, other host threads) race and must be serialised by the
+ * caller. Arguments and results are those of a11s_accept; `status` (nullable,
+ * device int32[2]) receives the device status word and its detail. Allocates
+ * nothing (no cudaMalloc, cudaFree or allocating library routine). */
+#define A11S_ACCEPT_STATIC_SCRATCH_BYTES (4u << 20)
+int a11s_accept_static(int32_t mode, int32_t dtype,
+                       const void *target_logits, const void *draft_logits, int64_t row_stride,
+                       float temperature, const float *uniforms,
+                       const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes,
+                       int32_t batch, int32_t max_nodes, int32_t vocab,
+                       int32_t *accept_len, int32_t *accepted_nodes, int32_t *accepted_tokens,
+                       int32_t *bonus, float *node_probs, int64_t *stats, int32_t *status,
+                       void *stream);
+
 /* ------------------------------------------------------------------------ K2
  * Tree-masked verification attention over the paged KV pool. Replaces the
  * decode attention of engine/pipeline.py:386-402 (GQA by repeat_interleave,
