@@ -16,6 +16,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(os.path.dirname(HERE), "include")
 OUT = os.path.join(HERE, "a11spec", "liba11spec.so")
+CPP = os.path.join(HERE, "cpp")
+VERIFIER_OUT = os.path.join(CPP, "libspec_verifier.so")
+CUDA_HOME = os.environ.get("CUDA_HOME", "/usr/local/cuda")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 NVCC_FLAGS = [
@@ -59,9 +62,27 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     return OUT
 
 
+def build_verifier(force: bool = False) -> str:
+    """libspec_verifier.so: the A11::Engine::SpeculativeTreeVerifier C++ interface
+    over liba11spec (g++, links liba11spec.so and the CUDA runtime)."""
+    src = os.path.join(CPP, "speculative_verifier.cpp")
+    hdr = os.path.join(CPP, "include", "engine", "speculative_verifier.hpp")
+    if not force and os.path.exists(VERIFIER_OUT) and all(
+            os.path.getmtime(p) <= os.path.getmtime(VERIFIER_OUT) for p in (src, hdr, OUT)):
+        return VERIFIER_OUT
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-I", os.path.join(CPP, "include"), "-I", INCLUDE,
+           "-I", os.path.join(CUDA_HOME, "include"), "-o", VERIFIER_OUT, src, "-L", os.path.dirname(OUT),
+           "-la11spec", "-Wl,-rpath,$ORIGIN/../a11spec", "-L", os.path.join(CUDA_HOME, "lib64"), "-lcudart"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError("g++ failed:\n" + r.stdout + r.stderr)
+    return VERIFIER_OUT
+
+
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     args = ap.parse_args()
     print(build(force=args.force, verbose=args.verbose))
+    print(build_verifier(force=args.force))

@@ -177,6 +177,24 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     return A11S_OK;
 }
 
+int a11s_verify_chain(const float *draft_probs, const float *target_probs, const float *uniforms,
+                      int32_t batch, int32_t n, int32_t *accepted_len, int32_t *last_idx,
+                      void *workspace, size_t workspace_bytes, void *stream) {
+    if (batch < 0 || n < 0) return fail(A11S_EINVAL, "a11s_verify_chain: negative size");
+    if (batch == 0) return A11S_OK;
+    if (!accepted_len || !last_idx || !workspace || (n > 0 && (!draft_probs || !target_probs || !uniforms)))
+        return fail(A11S_EINVAL, "a11s_verify_chain: null required pointer");
+    if (workspace_bytes < sizeof(a11s::StatusWord))
+        return fail(A11S_ENOSPACE, "a11s_verify_chain: workspace too small for the status word");
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(a11s::StatusWord), s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_verify_chain: clearing status");
+    e = a11s::launch_verify_chain(draft_probs, target_probs, uniforms, batch, n, accepted_len, last_idx,
+                                  static_cast<a11s::StatusWord *>(workspace), s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_verify_chain: launch");
+    return A11S_OK;
+}
+
 // ------------------------------------------------------------------- K4
 int a11s_kv_compact(void *k_pool, void *v_pool, int32_t num_layers, int64_t layer_stride,
                     int32_t num_pages, int32_t row_elems, int32_t elem_bytes, int32_t *page_table,

@@ -93,6 +93,9 @@ struct AttnArgs {
 
 cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s);
 
+cudaError_t launch_verify_chain(const float *draft, const float *target, const float *uni, int B, int n,
+                                int32_t *accepted_len, int32_t *last_idx, StatusWord *st, cudaStream_t s);
+
 // Records `msg` as this thread's a11s_last_error() and returns `code`.
 int set_error(int code, const char *msg);
 size_t tree_attention_partials_bytes(int32_t B, int32_t N, int32_t Hq, int32_t D, int32_t splits);

@@ -135,6 +135,22 @@ int a11s_accept(int32_t mode, int32_t dtype,
                 int32_t *bonus, float *node_probs, int64_t *stats,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/* Chain acceptance on per-token probabilities: the rule of
+ * SpeculativeTreeVerifier::verify_draft_tokens (src/engine/speculative_verifier.cpp:84-135)
+ * for `batch` independent chains of `n` drafts. draft, target, uniforms are
+ * fp32 device arrays [batch][n]; uniforms[b][i] judges draft i (the reference
+ * draws it from its thread_local std::mt19937(42), :65-69).
+ * Per draft: log space iff ld < 0 || lt < 0, then a = exp(max(lt - ld, -20))
+ * (this library's exp, relative error < 2e-6); otherwise ld = clamp(ld, 1e-10, 1),
+ * lt = clamp(lt, 0, 1 + 1e-6), a = lt / ld. a = min(a, 1); accept iff u < a;
+ * the first rejection ends the chain. accepted_len[b] and last_idx[b] (0 when
+ * nothing is accepted) are written; a chain whose target row holds NaN or Inf
+ * gets accepted_len = -1 and the status word ENONFINITE (the reference
+ * throws, :93-97). workspace >= 256 bytes (status word). */
+int a11s_verify_chain(const float *draft_probs, const float *target_probs, const float *uniforms,
+                      int32_t batch, int32_t n, int32_t *accepted_len, int32_t *last_idx,
+                      void *workspace, size_t workspace_bytes, void *stream);
+
 /* Fixed-scratch variant of a11s_accept, with no counterpart in the reference.
  * For callers that cannot pass a workspace because they may not allocate
  * device memory: hosts whose HBM is owned by another allocator that forbids

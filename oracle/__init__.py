@@ -67,6 +67,9 @@ def lib():
         L.or_accept.argtypes = [C.c_int32, _f32p, C.c_void_p, C.c_int64, C.c_float, C.c_void_p,
                                 _i32p, _i32p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                 _i32p, _i32p, _i32p, _i32p, C.c_void_p, C.c_void_p]
+        L.or_exp_neg.restype = C.c_float
+        L.or_exp_neg.argtypes = [C.c_float]
+        L.or_verify_chain.argtypes = [_f32p, _f32p, _f32p, C.c_int32, C.c_int32, _i32p, _i32p]
         L.or_tree_attention.argtypes = [_f32p, _f32p, _f32p, C.c_int32, _i32p, C.c_int32, _i32p,
                                         _i32p, C.c_void_p, C.c_int32, C.c_int32, C.c_int32,
                                         C.c_int32, C.c_int32, C.c_float, _f32p, C.c_void_p]
@@ -142,6 +145,18 @@ def accept(mode, target, tokens, parents, n_nodes=None, draft=None, temperature=
     out["status"] = rc
     out["stats"] = st
     return out
+
+
+def verify_chain(draft, target, uniforms):
+    """Chain rule of the reference verifier on [batch, n] per-token probabilities."""
+    d = np.ascontiguousarray(draft, dtype=np.float32)
+    t = np.ascontiguousarray(target, dtype=np.float32)
+    u = np.ascontiguousarray(uniforms, dtype=np.float32)
+    B, n = d.shape
+    al = np.zeros(B, np.int32)
+    li = np.zeros(B, np.int32)
+    rc = lib().or_verify_chain(d, t, u, B, n, al, li)
+    return al, li, rc
 
 
 # ----------------------------------------------------------------------------- attention

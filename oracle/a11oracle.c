@@ -443,6 +443,50 @@ int or_accept(int32_t mode, const float *target, const float *draft, int64_t row
 }
 
 /* ---------------------------------------------------------------------------
+ * Chain acceptance on per-token probabilities, src/engine/speculative_verifier.cpp:84-135.
+ * exp(x), x in [-20, 0): t = x*log2(e) rounded once, n = rint(t), 2^(t-n) by
+ * the same polynomial, 2^n added to the exponent field.
+ * ------------------------------------------------------------------------- */
+float or_exp_neg(float x) {
+    float t = x * 1.4426950408889634f;
+    float r = t + 12582912.0f;
+    float nf = r - 12582912.0f;
+    float f = t - nf;
+    int32_t n = (int32_t)nf;
+    float p = or_exp2_poly(f);
+    uint32_t bits = f2u(p) + ((uint32_t)n << 23);
+    float out; memcpy(&out, &bits, 4); return out;
+}
+
+int or_verify_chain(const float *draft, const float *target, const float *uniforms, int32_t batch,
+                    int32_t n, int32_t *accepted_len, int32_t *last_idx) {
+    int status = ST_OK;
+    for (int32_t b = 0; b < batch; ++b) {
+        const float *d = draft + (int64_t)b * n, *t = target + (int64_t)b * n, *u = uniforms + (int64_t)b * n;
+        int bad = 0;
+        for (int32_t i = 0; i < n; ++i) bad |= !(fabsf(t[i]) < INFINITY);
+        if (bad) { accepted_len[b] = -1; last_idx[b] = 0; status = status ? status : ST_ENONFINITE; continue; }
+        int32_t acc = 0, last = 0;
+        for (int32_t i = 0; i < n; ++i) {
+            float ld = d[i], lt = t[i], a;
+            if (ld < 0.0f || lt < 0.0f) {
+                float lr = fmaxf(lt - ld, -20.0f);
+                a = lr >= 0.0f ? 1.0f : or_exp_neg(lr);
+            } else {
+                ld = fmaxf(1e-10f, fminf(ld, 1.0f));
+                lt = fmaxf(0.0f, fminf(lt, 1.0f + 1e-6f));
+                a = lt / ld;
+            }
+            if (a > 1.0f) a = 1.0f;
+            if (u[i] < a) { ++acc; last = i; } else break;
+        }
+        accepted_len[b] = acc;
+        last_idx[b] = last;
+    }
+    return status;
+}
+
+/* ---------------------------------------------------------------------------
  * Tree attention, fp32. engine/pipeline.py:391-402: GQA head h reads KV head
  * h / (Hq/Hkv) (repeat_interleave), scores = q.k * scale in fp32, softmax in
  * fp32, probabilities rounded to bf16 before the PV product.

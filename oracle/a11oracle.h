@@ -39,6 +39,11 @@ int or_accept(int32_t mode, const float *target, const float *draft, int64_t row
               int32_t vocab, int32_t *accept_len, int32_t *accepted_nodes,
               int32_t *accepted_tokens, int32_t *bonus, float *node_probs, int64_t *stats);
 
+/* Chain acceptance on per-token probabilities (a11s_verify_chain). */
+float or_exp_neg(float x);
+int or_verify_chain(const float *draft, const float *target, const float *uniforms, int32_t batch,
+                    int32_t n, int32_t *accepted_len, int32_t *last_idx);
+
 /* Tree attention in fp32 (q, k_pool, v_pool given as fp32 widened from bf16). */
 int or_tree_attention(const float *q, const float *k_pool, const float *v_pool, int32_t num_pages,
                       const int32_t *page_table, int32_t max_pages_per_seq,
