@@ -58,6 +58,12 @@ def _load() -> C.CDLL:
     lib.a11s_ngram_expand.argtypes = [vp, i32, i32, vp, i32, i32, i32, i32, i32, vp, vp, vp, vp, vp]
     lib.a11s_ngram_bucket.restype = C.c_uint32
     lib.a11s_ngram_bucket.argtypes = [i32, i32, i32]
+    lib.a11s_verify_chain.argtypes = [vp, vp, vp, i32, i32, vp, vp, vp, sz, vp]
+    lib.a11s_accept_static.argtypes = [i32, i32, vp, vp, i64, f32, vp, vp, vp, vp, i32, i32, i32,
+                                       vp, vp, vp, vp, vp, vp, vp, vp]
+    for name in ("a11s_read_status", "a11s_accept", "a11s_tree_attention", "a11s_kv_compact",
+                 "a11s_ngram_expand", "a11s_verify_chain", "a11s_accept_static"):
+        getattr(lib, name).restype = C.c_int
     if lib.a11s_abi_version() != 1:
         raise ImportError("liba11spec.so ABI version mismatch")
     return lib
@@ -74,6 +80,6 @@ def check(rc: int) -> None:
 def symbols():
     """Names of every entry point declared in include/a11spec.h."""
     return ["a11s_abi_version", "a11s_last_error", "a11s_read_status",
-            "a11s_accept_workspace_bytes", "a11s_accept",
+            "a11s_accept_workspace_bytes", "a11s_accept", "a11s_accept_static",
             "a11s_tree_attention_workspace_bytes", "a11s_tree_attention", "a11s_kv_compact",
-            "a11s_ngram_expand", "a11s_ngram_bucket"]
+            "a11s_ngram_expand", "a11s_ngram_bucket", "a11s_verify_chain"]

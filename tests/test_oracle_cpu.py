@@ -301,5 +301,17 @@ def test_library_loads_and_exports_every_declared_symbol():
     lib = ctypes.CDLL(_lib.LIB_PATH)
     missing = [s for s in sorted(declared) if not hasattr(lib, s)]
     assert not missing, missing
-    assert declared <= set(_lib.symbols()) | declared
+    assert declared == set(_lib.symbols())
     assert lib.a11s_abi_version() == 1
+
+
+def test_every_entry_point_with_parameters_has_ctypes_argtypes():
+    """Undeclared argtypes make ctypes pass 64-bit pointers as 32-bit ints."""
+    from a11spec import _lib
+    hdr = open(os.path.join(ROOT, "include", "a11spec.h")).read()
+    for name, params in re.findall(r"\b(a11s_\w+)\s*\(([^)]*)\)", hdr):
+        f = getattr(_lib.lib, name)
+        if params.strip() in ("", "void"):
+            continue
+        assert f.argtypes is not None, name
+        assert len(f.argtypes) == len(params.split(",")), name
