@@ -1,11 +1,19 @@
 // accept.cu - K3: vocab-wide softmax/argmax + acceptance + path select + bonus draw.
 //
-// One kernel per call. Phase 1 (every block): warps stream 2048-token chunks
-// of the logits rows with 16-byte non-allocating loads, reduce each chunk with
-// warp shuffles and store a 16-byte chunk record (greedy: max, argmax; sampling:
-// max, frame, fixed-point exp sum). Phase 2 (the block that completes a
-// sequence, found with a fenced atomic counter, no waiting): walk the tree from
-// the root, draw the bonus token, write outputs and counters.
+// One kernel per call.
+// Phase 1 (every block, HBM-bound): warps stream 2048-token chunks of every
+//   live logits row with 16-byte non-allocating loads and keep one number per
+//   chunk: its maximum (NaN-propagating, so a NaN or +Inf is caught here).
+//   That is two instructions per logit, the single read of the vocab.
+// Phase 2 (the block that completes a sequence, found with a fenced atomic
+//   counter; nothing waits): walk the tree from the root.
+//   GREEDY  row argmax = first chunk holding the row max, then the first token
+//           equal to it inside that chunk (one 2048-token rescan per visited row).
+//   STOCH_* the fixed-point softmax statistics (frame c_j = ceil(cmax_j * k),
+//           S_j = sum of weights) are computed for the rows the walk visits only,
+//           by all 16 warps; then acceptance, residuals and the bonus draw.
+// The numbers are exactly those of the oracle (order-independent integer
+// sums), so decisions are bit-exact.
 //
 // Semantics: include/a11spec.h (a11s_accept). Reference behaviour followed:
 // src/engine/speculative_verifier.cpp:84-135 (acceptance rule, first rejection
@@ -15,126 +23,91 @@
 
 namespace a11s {
 
-constexpr int kWarps = 8;
+constexpr int kWarps = 16;
 constexpr int kThreads = kWarps * 32;
 constexpr int kMaxNch = A11S_MAX_VOCAB / A11S_CHUNK;  // 128
 
-// One 2048-token chunk of a row held in registers: 64 values per lane.
-// fp32: 16 x (4 floats), bf16: 8 x (8 bf16); vector i of lane covers tokens
-// [(i*32 + lane) * EPV, +EPV) of the chunk.
-template <bool BF16>
-struct Chunk {
-    static constexpr int EPV = BF16 ? 8 : 4;
-    static constexpr int NV = 64 / EPV;
-    uint4 d[NV];
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float r;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(r) : "f"(a), "f"(b));
+    return r;
+}
 
-    __device__ __forceinline__ void load(const void *row, int c0, int clen, int lane) {
+__device__ __forceinline__ float warp_max_nan(float v) {
 #pragma unroll
-        for (int i = 0; i < NV; ++i) {
-            const int e0 = (i * 32 + lane) * EPV;
-            if (e0 < clen) {
-                d[i] = ldg_stream(reinterpret_cast<const char *>(row) +
-                                  (size_t)(c0 + e0) * (BF16 ? 2 : 4));
-            } else {
-                const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
-                d[i] = make_uint4(ninf, ninf, ninf, ninf);
-            }
-        }
-    }
-    __device__ __forceinline__ float at(int i, int e) const {
-        const uint32_t w = (&d[i].x)[BF16 ? (e >> 1) : e];
+    for (int o = 16; o; o >>= 1) v = max_nan(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+template <bool BF16>
+struct Vec {
+    static constexpr int EPV = BF16 ? 8 : 4;  // logits per 16-byte vector
+    static constexpr int NV = 64 / EPV;       // vectors per lane per chunk
+    static constexpr int ESZ = BF16 ? 2 : 4;
+    __device__ static __forceinline__ float at(const uint4 &d, int e) {
+        const uint32_t w = (&d.x)[BF16 ? (e >> 1) : e];
         if (BF16) return (e & 1) ? bf16hi(w) : bf16lo(w);
         return __uint_as_float(w);
     }
 };
 
-__device__ __forceinline__ void argmax_merge(float &bv, int &bi, float ov, int oi) {
-    if (oi != INT_MAX && (bi == INT_MAX || ov > bv || (ov == bv && oi < bi))) {
-        bv = ov;
-        bi = oi;
-    }
-}
-
-__device__ __forceinline__ void warp_argmax(float &bv, int &bi) {
-#pragma unroll
-    for (int o = 16; o; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-        argmax_merge(bv, bi, ov, oi);
-    }
-}
-
-// ---------------------------------------------------------------------------
-// Phase 1 helpers: one chunk -> one record.
-// ---------------------------------------------------------------------------
+// Chunk max of one row chunk, lane layout: vector i of lane = logits
+// [(i*32 + lane) * EPV, +EPV). Positions past the row are -inf.
 template <bool BF16>
-__device__ __forceinline__ ChunkRec chunk_greedy(const void *row, int j, int V, int lane, int &bad) {
-    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-    Chunk<BF16> c;
-    c.load(row, c0, clen, lane);
-    float bv = -INFINITY;
-    int bi = INT_MAX;
-#pragma unroll
-    for (int i = 0; i < Chunk<BF16>::NV; ++i) {
-        const int e0 = (i * 32 + lane) * Chunk<BF16>::EPV;
-        if (e0 < clen) {
-#pragma unroll
-            for (int e = 0; e < Chunk<BF16>::EPV; ++e) {
-                const float v = c.at(i, e);
-                bad |= !(v < INFINITY);
-                if (v > bv || bi == INT_MAX) { bv = v; bi = c0 + e0 + e; }
-            }
-        }
-    }
-    warp_argmax(bv, bi);
-    ChunkRec r;
-    r.cmax = bv;
-    r.aux = bi;
-    r.sum = 0;
-    return r;
-}
-
-template <bool BF16>
-__device__ __forceinline__ ChunkRec chunk_stoch(const void *row, int j, int V, float k, int lane,
-                                                int &bad) {
-    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-    Chunk<BF16> c;
-    c.load(row, c0, clen, lane);
+__device__ __forceinline__ float chunk_max(const char *row, int c0, int clen, int lane) {
+    using VT = Vec<BF16>;
+    constexpr int G = 8;  // vectors in flight per lane
     float m = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < Chunk<BF16>::NV; ++i)
+    for (int i0 = 0; i0 < VT::NV; i0 += G) {
+        uint4 d[G];
 #pragma unroll
-        for (int e = 0; e < Chunk<BF16>::EPV; ++e) {
-            const float v = c.at(i, e);
-            bad |= !(v < INFINITY);
-            m = fmaxf(m, v);
+        for (int g = 0; g < G; ++g) {
+            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
         }
-    m = warp_fmax(m);
-    ChunkRec r;
-    r.cmax = m;
-    r.aux = A11S_FRAME_NONE;
-    r.sum = 0;
-    if (m == -INFINITY) return r;
-    const float mk = __fmul_rn(m, k);
-    if (!(fabsf(mk) < 16777216.0f)) { bad = 1; return r; }
-    const int cf = (int)ceilf(mk);
-    const float cff = (float)cf;
-    uint64_t s = 0;
 #pragma unroll
-    for (int i = 0; i < Chunk<BF16>::NV; ++i)
+        for (int g = 0; g < G; ++g)
 #pragma unroll
-        for (int e = 0; e < Chunk<BF16>::EPV; ++e) s += det_weight(c.at(i, e), k, cff);
-    r.aux = cf;
-    r.sum = warp_sum_u64(s);
-    return r;
+            for (int e = 0; e < VT::EPV; ++e) m = max_nan(m, VT::at(d[g], e));
+    }
+    return warp_max_nan(m);
 }
 
-__device__ __forceinline__ float load_logit(const void *row, int v, bool bf16) {
+// Sum of fixed-point weights of one chunk in frame cf (no max needed: the
+// frame comes from the phase-1 chunk max).
+template <bool BF16>
+__device__ __forceinline__ uint64_t chunk_wsum(const char *row, int c0, int clen, float k, float cf, int lane) {
+    using VT = Vec<BF16>;
+    constexpr int G = 4;
+    uint64_t s = 0;
+    for (int i0 = 0; i0 < VT::NV; i0 += G) {
+        uint4 d[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < VT::EPV; ++e) s += det_weight(VT::at(d[g], e), k, cf);
+    }
+    return warp_sum_u64(s);
+}
+
+__device__ __forceinline__ float load_logit(const char *row, int v, bool bf16) {
     if (bf16) {
         const uint16_t h = __ldg(reinterpret_cast<const unsigned short *>(row) + v);
         return __uint_as_float((uint32_t)h << 16);
     }
     return __ldg(reinterpret_cast<const float *>(row) + v);
+}
+
+__device__ __forceinline__ int32_t frame_of(float cmax, float k) {
+    return cmax == -INFINITY ? A11S_FRAME_NONE : (int32_t)ceilf(__fmul_rn(cmax, k));
 }
 
 // ---------------------------------------------------------------------------
@@ -147,8 +120,9 @@ struct RowStat {  // combined statistics of one row in the fixed-point softmax
 };
 
 struct WalkSmem {
-    int32_t fr[kMaxNch];    // p frames of the current node's row
-    uint64_t sub[kMaxNch];  // p chunk sums, rejected tokens removed (ONEHOT)
+    int32_t fr[kMaxNch];    // p frames of the current row
+    uint64_t sum[kMaxNch];  // p chunk sums of the current row
+    uint64_t sub[kMaxNch];  // p chunk sums with rejected tokens removed (ONEHOT)
     int32_t qfr[kMaxNch];   // q frames (DRAFT)
     uint64_t qsum[kMaxNch];
     uint64_t lvl[kMaxNch];  // chunk totals of the newest residual level (DRAFT)
@@ -156,30 +130,24 @@ struct WalkSmem {
     uint64_t T[A11S_MAX_WALK_LEVELS + 1];
     double invT[A11S_MAX_WALK_LEVELS + 1];
     int32_t excl[A11S_MAX_NODES];
+    float cp[A11S_CHUNK];   // one staged chunk of the p row (widened to fp32)
+    float cq[A11S_CHUNK];   // and of the q row (DRAFT)
     RowStat ps, qs;
     uint64_t S_eff;
     int32_t nexcl, L, node, alen, cpos, action, child, ok;
 };
 
-// Warp-cooperative combine of one row's chunk records (lanes stride chunks).
-// Writes frames/sums to smem arrays when given.
-__device__ RowStat combine_row(const ChunkRec *rec, int nch, int32_t *fr_out, uint64_t *sum_out,
-                               int lane) {
+__device__ RowStat combine_sums(const int32_t *fr, const uint64_t *sum, int nch, int lane) {
     int32_t C = A11S_FRAME_NONE;
-    for (int j = lane; j < nch; j += 32) {
-        const int32_t f = __ldcg(&rec[j].aux);
-        if (fr_out) fr_out[j] = f;
-        if (sum_out) sum_out[j] = __ldcg(&rec[j].sum);
-        if (f != A11S_FRAME_NONE) C = max(C, f);
-    }
+    for (int j = lane; j < nch; j += 32)
+        if (fr[j] != A11S_FRAME_NONE) C = max(C, fr[j]);
     C = warp_max(C);
     uint64_t S = 0;
     if (C != A11S_FRAME_NONE)
         for (int j = lane; j < nch; j += 32) {
-            const int32_t f = __ldcg(&rec[j].aux);
-            if (f == A11S_FRAME_NONE) continue;
-            const int d = C - f;
-            S += d > 63 ? 0ull : (__ldcg(&rec[j].sum) >> d);
+            if (fr[j] == A11S_FRAME_NONE) continue;
+            const int d = C - fr[j];
+            S += d > 63 ? 0ull : (sum[j] >> d);
         }
     S = warp_sum_u64(S);
     RowStat rs;
@@ -187,6 +155,25 @@ __device__ RowStat combine_row(const ChunkRec *rec, int nch, int32_t *fr_out, ui
     rs.S = S;
     rs.invS = S ? __ddiv_rn(1.0, __ull2double_rn(S)) : 0.0;
     return rs;
+}
+
+// Every warp of the block: frames and weight sums of one row into fr/sum.
+template <bool BF16>
+__device__ void row_sums(const char *row, const float *cmax, int nch, int V, float k, int32_t *fr, uint64_t *sum,
+                         int warp, int lane) {
+    for (int j = warp; j < nch; j += kWarps) {
+        const float cm = __ldcg(cmax + j);
+        const int32_t f = frame_of(cm, k);
+        uint64_t s = 0;
+        if (f != A11S_FRAME_NONE) {
+            const int c0 = j * A11S_CHUNK;
+            s = chunk_wsum<BF16>(row, c0, min(A11S_CHUNK, V - c0), k, (float)f, lane);
+        }
+        if (lane == 0) {
+            fr[j] = f;
+            sum[j] = s;
+        }
+    }
 }
 
 __device__ __forceinline__ double chunk_scale(const RowStat &rs, int32_t frame) {
@@ -217,16 +204,45 @@ __device__ __forceinline__ uint64_t level_weight(float p_prev, float q) {
     return __float2ull_rz(__fmul_rn(r, 0x1p40f));
 }
 
-// Inverse CDF inside one chunk, warp 0: lane l owns tokens [c0 + 64 l, +64).
-// wfn(v) gives the weight of token v. Returns the first token whose running
-// weight exceeds t2 (or the last positive-weight token).
+// Warp 0 copies one chunk of a row into shared memory as fp32 (coalesced
+// 16-byte loads, all in flight together); positions past the row get -inf.
+template <bool BF16>
+__device__ void stage_chunk(const char *row, int c0, int clen, float *dst, int lane) {
+    using VT = Vec<BF16>;
+    constexpr int NVW = A11S_CHUNK / (32 * VT::EPV);  // vectors per lane
+    constexpr int G = 8;                               // in flight per lane
+#pragma unroll
+    for (int i0 = 0; i0 < NVW; i0 += G) {
+        uint4 d[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < VT::EPV; ++e) dst[((i0 + g) * 32 + lane) * VT::EPV + e] = VT::at(d[g], e);
+    }
+    __syncwarp();
+}
+
+// Inverse CDF inside one staged chunk, warp 0: lane l owns tokens
+// [64 l, 64 l + 64) of the chunk. wfn(e) gives the weight of chunk position e
+// (read from shared memory; lanes read rotated positions to avoid bank
+// conflicts, integer sums make the order irrelevant). Returns the chunk
+// position of the first token whose running weight exceeds t2 (or the last
+// positive-weight position).
 template <typename WF>
-__device__ int scan_chunk(int c0, int clen, uint64_t t2, int lane, WF wfn) {
-    const int lo = lane * 64, hi = min(lo + 64, clen);
+__device__ int scan_chunk(int clen, uint64_t t2, int lane, WF wfn) {
+    const int lo = lane * 64;
     uint64_t mine = 0;
-    for (int e = lo; e < hi; ++e) mine += wfn(c0 + e);
-    // exclusive warp scan
-    uint64_t incl = mine;
+    for (int s = 0; s < 64; ++s) {
+        const int e = lo + ((s + lane) & 63);
+        if (e < clen) mine += wfn(e);
+    }
+    uint64_t incl = mine;  // inclusive warp scan
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
@@ -238,16 +254,15 @@ __device__ int scan_chunk(int c0, int clen, uint64_t t2, int lane, WF wfn) {
     int found = -1;
     if (here) {
         uint64_t acc = excl;
-        for (int e = lo; e < hi; ++e) {
-            acc += wfn(c0 + e);
-            if (acc > t2) { found = c0 + e; break; }
+        for (int e = lo; e < min(lo + 64, clen); ++e) {
+            acc += wfn(e);
+            if (acc > t2) { found = e; break; }
         }
     }
     if (who) return __shfl_sync(0xffffffffu, found, __ffs(who) - 1);
-    // t2 beyond the chunk total (cannot happen with consistent totals): last positive weight
-    int last = -1;
-    for (int e = lo; e < hi; ++e)
-        if (wfn(c0 + e)) last = c0 + e;
+    int last = -1;  // t2 beyond the chunk total (inconsistent totals): last positive weight
+    for (int e = lo; e < min(lo + 64, clen); ++e)
+        if (wfn(e)) last = e;
     return warp_max(last);
 }
 
@@ -272,17 +287,44 @@ __device__ __forceinline__ bool pick_chunk(float u, const uint64_t *A, const uin
     return true;
 }
 
+// Greedy argmax of a row (warp 0): first chunk holding the row max, then the
+// first token equal to it in that chunk (staged in shared memory).
+template <bool BF16>
+__device__ int row_argmax(const char *row, const float *cmax, int nch, int V, float *stage, int lane) {
+    float M = -INFINITY;
+    for (int j = lane; j < nch; j += 32) M = fmaxf(M, __ldcg(cmax + j));
+    M = warp_fmax(M);
+    int jstar = INT_MAX;
+    for (int j0 = 0; j0 < nch && jstar == INT_MAX; j0 += 32) {
+        const int j = j0 + lane;
+        const unsigned hit = __ballot_sync(0xffffffffu, j < nch && __ldcg(cmax + j) == M);
+        if (hit) jstar = j0 + __ffs(hit) - 1;
+    }
+    if (jstar == INT_MAX) return 0;  // unreachable for rows without NaN
+    const int c0 = jstar * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+    stage_chunk<BF16>(row, c0, clen, stage, lane);
+    int first = INT_MAX;  // smallest position equal to M (rotated reads, order-free min)
+    for (int s = 0; s < 64; ++s) {
+        const int e = lane * 64 + ((s + lane) & 63);
+        if (e < clen && stage[e] == M) first = min(first, e);
+    }
+    first = -warp_max(-first);  // warp min
+    __syncwarp();
+    return c0 + (first == INT_MAX ? 0 : first);
+}
+
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
 template <int MODE, bool BF16>
-__global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
+__global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a) {
     const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
     const bool seq_ok = n_live >= 1 && n_live <= a.N;
     if (!seq_ok) n_live = 0;
+    const size_t row_bytes = (size_t)a.stride * (BF16 ? 2 : 4);
 
-    // ---------------- phase 1: chunk records ----------------
+    // ---------------- phase 1: chunk maxima ----------------
     const int u0 = blockIdx.x * a.slice, u1 = min(u0 + a.slice, a.units_per_seq);
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += kWarps) {
@@ -290,11 +332,12 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
         const bool isq = r >= a.N;
         const int node = isq ? r - a.N : r;
         if (node >= n_live) continue;
-        const char *base = reinterpret_cast<const char *>(isq ? a.draft : a.target);
-        const void *row = base + ((size_t)b * a.N + node) * (size_t)a.stride * (BF16 ? 2 : 4);
-        ChunkRec rec = MODE == A11S_ACCEPT_GREEDY ? chunk_greedy<BF16>(row, j, a.V, lane, bad)
-                                                  : chunk_stoch<BF16>(row, j, a.V, a.k, lane, bad);
-        if (lane == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = rec;
+        const char *row = reinterpret_cast<const char *>(isq ? a.draft : a.target) + ((size_t)b * a.N + node) * row_bytes;
+        const int c0 = j * A11S_CHUNK;
+        const float m = chunk_max<BF16>(row, c0, min(A11S_CHUNK, a.V - c0), lane);
+        bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
+        if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
+        if (lane == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = m;
     }
     if (warp_or(bad) && lane == 0) report(a.status, A11S_ENONFINITE, b);
     __threadfence();
@@ -316,9 +359,7 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
     const int32_t *par = a.parents + (size_t)b * N;
     int32_t *an = a.acc_nodes + (size_t)b * N;
     int32_t *at = a.acc_tokens + (size_t)b * N;
-    const ChunkRec *recs_b = a.recs + (size_t)b * a.rows_per_seq * nch;
-    const bool bf16 = BF16;
-    const size_t row_bytes = (size_t)a.stride * (BF16 ? 2 : 4);
+    const float *cmax_b = a.recs + (size_t)b * a.rows_per_seq * nch;
     const char *tgt_b = reinterpret_cast<const char *>(a.target) + (size_t)b * N * row_bytes;
     const char *drf_b = MODE == A11S_ACCEPT_STOCH_DRAFT
                             ? reinterpret_cast<const char *>(a.draft) + (size_t)b * N * row_bytes
@@ -343,18 +384,26 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
         return;
     }
 
-    // node probabilities p(tokens[i]) in the parent's row (sampling modes)
+    // node probabilities p(tokens[i]) in the parent's row (sampling modes, optional):
+    // one statistics pass per row that has children
     if (MODE != A11S_ACCEPT_GREEDY && a.node_probs) {
-        for (int i = 1 + warp; i < n_live; i += kWarps) {
-            const int pr = par[i];
-            const ChunkRec *rr = recs_b + (size_t)pr * nch;
-            const RowStat rs = combine_row(rr, nch, nullptr, nullptr, lane);
-            if (lane == 0) {
-                const int x = tok[i], j = x / A11S_CHUNK;
-                const int32_t f = __ldcg(&rr[j].aux);
-                const float l = load_logit(tgt_b + (size_t)pr * row_bytes, x, bf16);
-                a.node_probs[(size_t)b * N + i] = prob_of(l, a.k, f, chunk_scale(rs, f));
+        for (int r = 0; r < n_live; ++r) {
+            bool has_child = false;
+            for (int c = r + 1; c < n_live && !has_child; ++c) has_child = par[c] == r;
+            if (!has_child) continue;
+            const char *prow = tgt_b + (size_t)r * row_bytes;
+            row_sums<BF16>(prow, cmax_b + (size_t)r * nch, nch, V, a.k, sm.fr, sm.sum, warp, lane);
+            __syncthreads();
+            if (warp == 0) {
+                const RowStat rs = combine_sums(sm.fr, sm.sum, nch, lane);
+                for (int c = r + 1 + lane; c < n_live; c += 32) {
+                    if (par[c] != r) continue;
+                    const int x = tok[c], j = x / A11S_CHUNK;
+                    a.node_probs[(size_t)b * N + c] = prob_of(load_logit(prow, x, BF16), a.k, sm.fr[j],
+                                                              chunk_scale(rs, sm.fr[j]));
+                }
             }
+            __syncthreads();
         }
     }
 
@@ -363,39 +412,43 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
     if (MODE == A11S_ACCEPT_GREEDY) {
         if (warp == 0) {
             for (;;) {
-                const ChunkRec *rr = recs_b + (size_t)node * nch;
-                float bv = -INFINITY;
-                int bi = INT_MAX;
-                for (int j = lane; j < nch; j += 32) argmax_merge(bv, bi, __ldcg(&rr[j].cmax), __ldcg(&rr[j].aux));
-                warp_argmax(bv, bi);
+                const int am = row_argmax<BF16>(tgt_b + (size_t)node * row_bytes, cmax_b + (size_t)node * nch, nch,
+                                                V, sm.cp, lane);
                 int next = INT_MAX;
                 for (int c0 = node + 1; c0 < n_live && next == INT_MAX; c0 += 32) {
                     const int c = c0 + lane;
-                    const bool hit = c < n_live && par[c] == node && tok[c] == bi;
-                    const unsigned m = __ballot_sync(0xffffffffu, hit);
+                    const unsigned m = __ballot_sync(0xffffffffu, c < n_live && par[c] == node && tok[c] == am);
                     if (m) next = c0 + __ffs(m) - 1;
                 }
-                if (next == INT_MAX) { bonus = bi; break; }
+                if (next == INT_MAX) { bonus = am; break; }
                 if (lane == 0) { an[alen] = next; at[alen] = tok[next]; }
                 ++alen;
                 node = next;
             }
         }
     } else {
-        // Sampling walk: warp 0 decides, every warp helps with residual passes.
+        // Sampling walk: warp 0 decides; every warp computes row statistics and residual passes.
         if (threadIdx.x == 0) { sm.node = 0; sm.alen = 0; }
         __syncthreads();
         for (;;) {  // one iteration per visited node
+            const int nd = sm.node;
+            row_sums<BF16>(tgt_b + (size_t)nd * row_bytes, cmax_b + (size_t)nd * nch, nch, V, a.k, sm.fr, sm.sum,
+                           warp, lane);
+            if (MODE == A11S_ACCEPT_STOCH_DRAFT)
+                row_sums<BF16>(drf_b + (size_t)nd * row_bytes, cmax_b + (size_t)(N + nd) * nch, nch, V, a.k, sm.qfr,
+                               sm.qsum, warp, lane);
+            __syncthreads();
             if (warp == 0) {
-                node = sm.node;
-                sm.ps = combine_row(recs_b + (size_t)node * nch, nch, sm.fr, sm.sub, lane);
-                if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                    sm.qs = combine_row(recs_b + (size_t)(N + node) * nch, nch, sm.qfr, sm.qsum, lane);
+                sm.ps = combine_sums(sm.fr, sm.sum, nch, lane);
+                if (MODE == A11S_ACCEPT_STOCH_DRAFT) sm.qs = combine_sums(sm.qfr, sm.qsum, nch, lane);
+                for (int j = lane; j < nch; j += 32) sm.sub[j] = sm.sum[j];
+                __syncwarp();
                 if (lane == 0) {
                     sm.S_eff = sm.ps.S;
                     sm.nexcl = 0;
                     sm.L = 0;
-                    sm.cpos = node;
+                    sm.cpos = nd;
+                    sm.action = 0;
                     if (sm.ps.S == 0 || (MODE == A11S_ACCEPT_STOCH_DRAFT && sm.qs.S == 0)) {
                         report(a.status, A11S_ENONFINITE, b);
                         sm.action = 3;  // abort
@@ -426,8 +479,7 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                             sm.child = next;
                             const int x = tok[next], j = x / A11S_CHUNK;
                             const float u = a.uniforms[(size_t)b * N + next];
-                            const float lx = load_logit(tgt_b + (size_t)sm.node * row_bytes, x, bf16);
-                            const uint64_t wx = det_weight(lx, a.k, (float)sm.fr[j]);
+                            const float lx = load_logit(tgt_b + (size_t)sm.node * row_bytes, x, BF16);
                             if (MODE == A11S_ACCEPT_STOCH_ONEHOT) {
                                 bool ex = false;
                                 for (int e = 0; e < sm.nexcl; ++e) ex |= sm.excl[e] == x;
@@ -444,7 +496,7 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                                     sm.action = 2;
                                     if (!ex) {
                                         sm.excl[sm.nexcl++] = x;
-                                        if (sm.fr[j] != A11S_FRAME_NONE) sm.sub[j] -= wx;
+                                        if (sm.fr[j] != A11S_FRAME_NONE) sm.sub[j] -= det_weight(lx, a.k, (float)sm.fr[j]);
                                         uint64_t S = 0;
                                         for (int jj = 0; jj < nch; ++jj) {
                                             if (sm.fr[jj] == A11S_FRAME_NONE) continue;
@@ -456,7 +508,7 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                                 }
                             } else {
                                 const float p0 = prob_of(lx, a.k, sm.fr[j], chunk_scale(sm.ps, sm.fr[j]));
-                                const float lq = load_logit(drf_b + (size_t)sm.node * row_bytes, x, bf16);
+                                const float lq = load_logit(drf_b + (size_t)sm.node * row_bytes, x, BF16);
                                 const float qx = prob_of(lq, a.k, sm.qfr[j], chunk_scale(sm.qs, sm.qfr[j]));
                                 const float lt = level_prob(p0, qx, sm.L, sm.invT);
                                 sm.action = accept_linear(u, lt, qx) ? 1 : (sm.L < A11S_MAX_WALK_LEVELS ? 4 : 2);
@@ -485,7 +537,7 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                     const char *prow = tgt_b + (size_t)sm.node * row_bytes;
                     const char *qrow = drf_b + (size_t)sm.node * row_bytes;
                     const int L = sm.L;
-                    constexpr int EPV = Chunk<BF16>::EPV, NV = Chunk<BF16>::NV, G = 4;
+                    constexpr int EPV = Vec<BF16>::EPV, NV = Vec<BF16>::NV, G = 4;
                     for (int j = warp; j < nch; j += kWarps) {
                         const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
                         const int32_t fp = sm.fr[j], fq = sm.qfr[j];
@@ -505,12 +557,8 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                             for (int g = 0; g < G; ++g)
 #pragma unroll
                                 for (int e = 0; e < EPV; ++e) {
-                                    const uint32_t wp = (&vp[g].x)[BF16 ? (e >> 1) : e];
-                                    const uint32_t wq = (&vq[g].x)[BF16 ? (e >> 1) : e];
-                                    const float lp = BF16 ? ((e & 1) ? bf16hi(wp) : bf16lo(wp)) : __uint_as_float(wp);
-                                    const float lq = BF16 ? ((e & 1) ? bf16hi(wq) : bf16lo(wq)) : __uint_as_float(wq);
-                                    const float pv = prob_of(lp, a.k, fp, scp);
-                                    const float qv = prob_of(lq, a.k, fq, scq);
+                                    const float pv = prob_of(Vec<BF16>::at(vp[g], e), a.k, fp, scp);
+                                    const float qv = prob_of(Vec<BF16>::at(vq[g], e), a.k, fq, scq);
                                     s += level_weight(level_prob(pv, qv, L, sm.invT), qv);
                                 }
                         }
@@ -553,18 +601,20 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                     const double scp = chunk_scale(sm.ps, fp), scq = chunk_scale(sm.qs, fq);
                     const int L = sm.L;
                     const float k = a.k;
-                    bonus = scan_chunk(j * A11S_CHUNK, min(A11S_CHUNK, V - j * A11S_CHUNK), t2, lane,
-                                       [&](int v) {
-                                           const float pv = prob_of(load_logit(prow, v, bf16), k, fp, scp);
-                                           const float qv = prob_of(load_logit(qrow, v, bf16), k, fq, scq);
-                                           return level_weight(level_prob(pv, qv, L - 1, sm.invT), qv);
-                                       });
+                    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+                    stage_chunk<BF16>(prow, c0, clen, sm.cp, lane);
+                    stage_chunk<BF16>(qrow, c0, clen, sm.cq, lane);
+                    bonus = c0 + scan_chunk(clen, t2, lane, [&](int e) {
+                                const float pv = prob_of(sm.cp[e], k, fp, scp);
+                                const float qv = prob_of(sm.cq[e], k, fq, scq);
+                                return level_weight(level_prob(pv, qv, L - 1, sm.invT), qv);
+                            });
                 }
             } else {
                 const bool use_excl = MODE == A11S_ACCEPT_STOCH_ONEHOT && sm.S_eff != 0;
                 // A_j in the row frame, local totals Lc_j (sm.tmp / sm.lvl as scratch)
                 for (int jj = lane; jj < nch; jj += 32) {
-                    const uint64_t loc = use_excl ? sm.sub[jj] : __ldcg(&recs_b[(size_t)nd * nch + jj].sum);
+                    const uint64_t loc = use_excl ? sm.sub[jj] : sm.sum[jj];
                     sm.tmp[jj] = loc;
                     const int32_t f = sm.fr[jj];
                     const int d = sm.ps.C - f;
@@ -579,12 +629,13 @@ __global__ void __launch_bounds__(kThreads) accept_kernel(const AcceptArgs a) {
                     const float cff = (float)sm.fr[j];
                     const float k = a.k;
                     const int nex = use_excl ? sm.nexcl : 0;
-                    bonus = scan_chunk(j * A11S_CHUNK, min(A11S_CHUNK, V - j * A11S_CHUNK), t2, lane,
-                                       [&](int v) -> uint64_t {
-                                           for (int e = 0; e < nex; ++e)
-                                               if (sm.excl[e] == v) return 0ull;
-                                           return det_weight(load_logit(prow, v, bf16), k, cff);
-                                       });
+                    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+                    stage_chunk<BF16>(prow, c0, clen, sm.cp, lane);
+                    bonus = c0 + scan_chunk(clen, t2, lane, [&](int e) -> uint64_t {
+                                for (int x = 0; x < nex; ++x)
+                                    if (sm.excl[x] == c0 + e) return 0ull;
+                                return det_weight(sm.cp[e], k, cff);
+                            });
                 }
             }
             alen = sm.alen;

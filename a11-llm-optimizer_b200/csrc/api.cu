@@ -57,7 +57,7 @@ AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32
     const size_t rows = (size_t)batch * max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
     L.counters = kHeaderBytes;
     L.recs = L.counters + up256(sizeof(int32_t) * (size_t)batch);
-    L.total = L.recs + up256(rows * nch * sizeof(a11s::ChunkRec));
+    L.total = L.recs + up256(rows * nch * sizeof(float));
     return L;
 }
 
@@ -156,15 +156,15 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     char *ws = static_cast<char *>(workspace);
     a.status = reinterpret_cast<a11s::StatusWord *>(ws);
     a.counters = reinterpret_cast<int32_t *>(ws + L.counters);
-    a.recs = reinterpret_cast<a11s::ChunkRec *>(ws + L.recs);
+    a.recs = reinterpret_cast<float *>(ws + L.recs);
 
-    // Balance: about 4 waves of 3 resident 256-thread blocks per SM, at least
-    // 8 chunks (one per warp) per block.
+    // Balance: about 4 waves of 2 resident 512-thread blocks per SM, at least
+    // 16 chunks (one per warp) per block.
     const long long total_units = (long long)batch * a.units_per_seq;
-    const long long target_blocks = (long long)sm_count() * 3 * 4;
+    const long long target_blocks = (long long)sm_count() * 2 * 4;
     long long slice = (total_units + target_blocks - 1) / target_blocks;
-    slice = ((slice + 7) / 8) * 8;
-    if (slice < 8) slice = 8;
+    slice = ((slice + 15) / 16) * 16;
+    if (slice < 16) slice = 16;
     if (slice > a.units_per_seq) slice = a.units_per_seq;
     a.slice = (int32_t)slice;
     const int grid_x = (a.units_per_seq + a.slice - 1) / a.slice;

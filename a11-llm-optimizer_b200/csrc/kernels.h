@@ -7,15 +7,6 @@ namespace a11s {
 
 struct StatusWord;
 
-// 16-byte record of one 2048-token chunk of one logits row.
-// greedy: cmax = chunk max, aux = argmax token (lowest index on ties);
-// sampling: cmax = chunk max, aux = frame c_j (INT32_MIN if all -inf), sum = S_j.
-struct __align__(16) ChunkRec {
-    float cmax;
-    int32_t aux;
-    unsigned long long sum;
-};
-
 struct AcceptArgs {
     const void *target;
     const void *draft;
@@ -32,7 +23,7 @@ struct AcceptArgs {
     int32_t *bonus;
     float *node_probs;
     long long *stats;
-    ChunkRec *recs;
+    float *recs;  // [B][rows_per_seq][nch] chunk maxima (NaN-propagating)
     int32_t *counters;
     StatusWord *status;
 };

@@ -397,9 +397,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     const float a0 = tc::ex2(fmaf(x[col], sl2, neg));
                     const float a1 = tc::ex2(fmaf(x[col + 1], sl2, neg));
                     w[e] = pack_bf16x2(a0, a1);
-                    // the row sum uses the bf16 values the PV product sees
-                    ls[(2 * e) & 7] += __uint_as_float(w[e] << 16);
-                    ls[(2 * e + 1) & 7] += __uint_as_float(w[e] & 0xFFFF0000u);
+                    ls[(2 * e) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
+                    ls[(2 * e + 1) & 7] += a1;
                 }
                 *reinterpret_cast<uint4 *>(prow + ((c ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
             }

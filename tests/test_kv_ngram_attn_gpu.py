@@ -134,7 +134,8 @@ def _attn_case(seed, B, N, Hq, Hkv, ctx, dev, ragged=True):
     kv = W.paged_kv(B, ctx, N, Hkv, 128, P, seed=seed, device=dev)
     if ragged:  # different context lengths per sequence
         kv["ctx_lens"] = torch.as_tensor(rng.integers(max(1, ctx - 40), ctx + 1, B), dtype=torch.int32, device=dev)
-    q = torch.randn(B, N, Hq, 128, device=dev).to(torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(seed)
+    q = torch.randn(B, N, Hq, 128, device=dev, generator=g).to(torch.bfloat16)
     nn = np.array([N if b % 2 == 0 else max(1, N - 3 * b) for b in range(B)], np.int32)
     return q, kv, parents, nn
 
