@@ -129,13 +129,62 @@ struct WalkSmem {
     uint64_t tmp[kMaxNch];
     uint64_t T[A11S_MAX_WALK_LEVELS + 1];
     double invT[A11S_MAX_WALK_LEVELS + 1];
-    int32_t excl[A11S_MAX_NODES];
+    int32_t excl[A11S_MAX_ACCEPT_NODES];
+    int32_t tok[A11S_MAX_ACCEPT_NODES];   // the sequence's tree and uniforms, staged once
+    int32_t par[A11S_MAX_ACCEPT_NODES];
+    float uni[A11S_MAX_ACCEPT_NODES];
+    int32_t kids[A11S_MAX_ACCEPT_NODES];  // children of the current node, index order
+    float kl[A11S_MAX_ACCEPT_NODES];      // their target logits
+    float kq[A11S_MAX_ACCEPT_NODES];      // and draft logits (DRAFT)
     float cp[A11S_CHUNK];   // one staged chunk of the p row (widened to fp32)
     float cq[A11S_CHUNK];   // and of the q row (DRAFT)
+    uint64_t wtot[kWarps];  // per-warp weight totals of the bonus scan
     RowStat ps, qs;
-    uint64_t S_eff;
-    int32_t nexcl, L, node, alen, cpos, action, child, ok;
+    uint64_t S_eff, bt2;
+    int32_t nexcl, L, node, alen, ck, nk, action, child, ok, bj, res[2];
 };
+
+// Inverse CDF inside one chunk, every thread of the block: thread t owns the
+// chunk positions [4 t, 4 t + 4) and wfn(pos, w) fills their four weights.
+// Returns (to every thread) the first position whose running weight exceeds
+// t2; if t2 is beyond the chunk total (inconsistent totals), the last
+// positive-weight position; -1 if there is none.
+template <typename WF>
+__device__ int block_scan_chunk(int clen, uint64_t t2, WF wfn, WalkSmem &sm) {
+    static_assert(A11S_CHUNK == 4 * kThreads, "four chunk positions per thread");
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, p0 = 4 * threadIdx.x;
+    uint64_t w[4] = {0ull, 0ull, 0ull, 0ull};
+    if (p0 < clen) wfn(p0, w);
+    const uint64_t mine = w[0] + w[1] + w[2] + w[3];
+    uint64_t incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+    }
+    if (lane == 31) sm.wtot[warp] = incl;
+    if (threadIdx.x == 0) {
+        sm.res[0] = INT_MAX;
+        sm.res[1] = -1;
+    }
+    __syncthreads();
+    uint64_t acc = incl - mine;
+    for (int i = 0; i < warp; ++i) acc += sm.wtot[i];
+    if (acc <= t2 && t2 - acc < mine) {  // at most one thread
+        for (int e = 0; e < 4; ++e) {
+            acc += w[e];
+            if (acc > t2) { sm.res[0] = p0 + e; break; }
+        }
+    }
+    int last = -1;
+#pragma unroll
+    for (int e = 0; e < 4; ++e)
+        if (w[e]) last = p0 + e;
+    last = warp_max(last);
+    if (lane == 0 && last >= 0) atomicMax(&sm.res[1], last);
+    __syncthreads();
+    return sm.res[0] != INT_MAX ? sm.res[0] : sm.res[1];
+}
 
 __device__ RowStat combine_sums(const int32_t *fr, const uint64_t *sum, int nch, int lane) {
     int32_t C = A11S_FRAME_NONE;
@@ -173,6 +222,21 @@ __device__ void row_sums(const char *row, const float *cmax, int nch, int V, flo
             fr[j] = f;
             sum[j] = s;
         }
+    }
+}
+
+// Frames and weight sums of a row: the root's come from phase 1, the others
+// are computed by every warp of the block.
+template <bool BF16>
+__device__ void row_stats_into(const char *row, const float *cmax, const unsigned long long *root, int nch, int V,
+                               float k, int32_t *fr, uint64_t *sum, int warp, int lane) {
+    if (root) {
+        for (int j = threadIdx.x; j < nch; j += blockDim.x) {
+            fr[j] = frame_of(__ldcg(cmax + j), k);
+            sum[j] = __ldcg(root + j);
+        }
+    } else {
+        row_sums<BF16>(row, cmax, nch, V, k, fr, sum, warp, lane);
     }
 }
 
@@ -228,63 +292,65 @@ __device__ void stage_chunk(const char *row, int c0, int clen, float *dst, int l
     __syncwarp();
 }
 
-// Inverse CDF inside one staged chunk, warp 0: lane l owns tokens
-// [64 l, 64 l + 64) of the chunk. wfn(e) gives the weight of chunk position e
-// (read from shared memory; lanes read rotated positions to avoid bank
-// conflicts, integer sums make the order irrelevant). Returns the chunk
-// position of the first token whose running weight exceeds t2 (or the last
-// positive-weight position).
-template <typename WF>
-__device__ int scan_chunk(int clen, uint64_t t2, int lane, WF wfn) {
-    const int lo = lane * 64;
-    uint64_t mine = 0;
-    for (int s = 0; s < 64; ++s) {
-        const int e = lo + ((s + lane) & 63);
-        if (e < clen) mine += wfn(e);
+// Four logits at chunk-relative position pos (a multiple of 4; rows are
+// 16-byte aligned and the vocab a multiple of the vector width, so the
+// four stay inside the row).
+template <bool BF16>
+__device__ __forceinline__ void load4(const char *row, int pos, float v[4]) {
+    if (BF16) {
+        const uint2 d = __ldg(reinterpret_cast<const uint2 *>(row + (size_t)pos * 2));
+        v[0] = bf16lo(d.x); v[1] = bf16hi(d.x); v[2] = bf16lo(d.y); v[3] = bf16hi(d.y);
+    } else {
+        const uint4 d = __ldg(reinterpret_cast<const uint4 *>(row + (size_t)pos * 4));
+        v[0] = __uint_as_float(d.x); v[1] = __uint_as_float(d.y);
+        v[2] = __uint_as_float(d.z); v[3] = __uint_as_float(d.w);
     }
-    uint64_t incl = mine;  // inclusive warp scan
+}
+
+// Chunk selection of the two-level inverse CDF (warp 0): t = floor(u * sum A),
+// j = first chunk whose inclusive prefix of A exceeds t, t2 = floor((t -
+// prefix_before_j) * Lc_j / A_j). Lane l owns chunks [4 l, 4 l + 4).
+__device__ bool pick_chunk(float u, const uint64_t *A, const uint64_t *Lc, int nch, int lane, int &j_out,
+                           uint64_t &t2_out) {
+    static_assert(A11S_MAX_VOCAB / A11S_CHUNK <= 4 * 32, "four chunks per lane");
+    uint64_t a4[4], mine = 0;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+        const int j = 4 * lane + g;
+        a4[g] = j < nch ? A[j] : 0ull;
+        mine += a4[g];
+    }
+    uint64_t incl = mine;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
         const uint64_t y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
     }
-    const uint64_t excl = incl - mine;
-    const bool here = excl <= t2 && t2 < incl;
-    const unsigned who = __ballot_sync(0xffffffffu, here);
-    int found = -1;
-    if (here) {
-        uint64_t acc = excl;
-        for (int e = lo; e < min(lo + 64, clen); ++e) {
-            acc += wfn(e);
-            if (acc > t2) { found = e; break; }
-        }
-    }
-    if (who) return __shfl_sync(0xffffffffu, found, __ffs(who) - 1);
-    int last = -1;  // t2 beyond the chunk total (inconsistent totals): last positive weight
-    for (int e = lo; e < min(lo + 64, clen); ++e)
-        if (wfn(e)) last = e;
-    return warp_max(last);
-}
-
-// Chunk selection of the two-level inverse CDF (lane 0 of warp 0).
-__device__ __forceinline__ bool pick_chunk(float u, const uint64_t *A, const uint64_t *Lc, int nch,
-                                           int &j_out, uint64_t &t2_out) {
-    uint64_t tot = 0;
-    for (int j = 0; j < nch; ++j) tot += A[j];
+    const uint64_t tot = __shfl_sync(0xffffffffu, incl, 31);
     if (tot == 0) return false;
     uint64_t t = __double2ull_rz(__dmul_rn((double)u, __ull2double_rn(tot)));
     if (t >= tot) t = tot - 1;
-    uint64_t acc = 0;
-    int j = 0;
-    for (; j < nch; ++j) {
-        if (acc + A[j] > t) break;
-        acc += A[j];
+    uint64_t acc = incl - mine;
+    const bool here = acc <= t && t - acc < mine;
+    int j = -1;
+    uint64_t t2 = 0;
+    if (here) {
+#pragma unroll
+        for (int g = 0; g < 4; ++g) {
+            if (j < 0 && acc + a4[g] > t) {
+                j = 4 * lane + g;
+                const unsigned __int128 prod = (unsigned __int128)(t - acc) * Lc[j];
+                t2 = (uint64_t)(prod / a4[g]);
+            }
+            if (j < 0) acc += a4[g];
+        }
     }
-    if (j >= nch) return false;
-    const unsigned __int128 prod = (unsigned __int128)(t - acc) * Lc[j];
-    t2_out = (uint64_t)(prod / A[j]);
-    j_out = j;
-    return true;
+    const unsigned who = __ballot_sync(0xffffffffu, here);
+    if (!who) return false;  // unreachable: t < tot
+    const int src = __ffs(who) - 1;
+    j_out = __shfl_sync(0xffffffffu, j, src);
+    t2_out = __shfl_sync(0xffffffffu, t2, src);
+    return j_out >= 0;
 }
 
 // Greedy argmax of a row (warp 0): first chunk holding the row max, then the
@@ -328,16 +394,23 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     const int u0 = blockIdx.x * a.slice, u1 = min(u0 + a.slice, a.units_per_seq);
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += kWarps) {
-        const int r = u / a.nch, j = u - r * a.nch;
+        const int j = u / a.rows_per_seq, r = u - j * a.rows_per_seq;  // rows fastest
         const bool isq = r >= a.N;
         const int node = isq ? r - a.N : r;
         if (node >= n_live) continue;
         const char *row = reinterpret_cast<const char *>(isq ? a.draft : a.target) + ((size_t)b * a.N + node) * row_bytes;
-        const int c0 = j * A11S_CHUNK;
-        const float m = chunk_max<BF16>(row, c0, min(A11S_CHUNK, a.V - c0), lane);
+        const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, a.V - c0);
+        const float m = chunk_max<BF16>(row, c0, clen, lane);
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
         if (lane == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = m;
+        if (MODE != A11S_ACCEPT_GREEDY && node == 0) {
+            // The walk always starts at the root: its weight sums are taken
+            // here, while the chunk is hot in L2, instead of in the walk.
+            const int32_t f = m < INFINITY ? frame_of(m, a.k) : A11S_FRAME_NONE;
+            const uint64_t s = f == A11S_FRAME_NONE ? 0ull : chunk_wsum<BF16>(row, c0, clen, a.k, (float)f, lane);
+            if (lane == 0) a.root_sums[((size_t)b * 2 + (isq ? 1 : 0)) * a.nch + j] = s;
+        }
     }
     if (warp_or(bad) && lane == 0) report(a.status, A11S_ENONFINITE, b);
     __threadfence();
@@ -355,8 +428,6 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // ---------------- phase 2: walk ----------------
     __shared__ WalkSmem sm;
     const int N = a.N, V = a.V, nch = a.nch;
-    const int32_t *tok = a.tokens + (size_t)b * N;
-    const int32_t *par = a.parents + (size_t)b * N;
     int32_t *an = a.acc_nodes + (size_t)b * N;
     int32_t *at = a.acc_tokens + (size_t)b * N;
     const float *cmax_b = a.recs + (size_t)b * a.rows_per_seq * nch;
@@ -364,11 +435,17 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     const char *drf_b = MODE == A11S_ACCEPT_STOCH_DRAFT
                             ? reinterpret_cast<const char *>(a.draft) + (size_t)b * N * row_bytes
                             : nullptr;
-
+    // stage the tree (and uniforms) once: every later lookup is a shared-memory read
+    for (int i = threadIdx.x; i < n_live; i += blockDim.x) {
+        sm.tok[i] = a.tokens[(size_t)b * N + i];
+        sm.par[i] = a.parents[(size_t)b * N + i];
+        if (MODE != A11S_ACCEPT_GREEDY) sm.uni[i] = a.uniforms[(size_t)b * N + i];
+    }
+    __syncthreads();
     if (warp == 0) {
         int okl = seq_ok ? 1 : 0;
         for (int i = 1 + lane; i < n_live; i += 32)
-            if (par[i] < 0 || par[i] >= i || tok[i] < 0 || tok[i] >= V) okl = 0;
+            if (sm.par[i] < 0 || sm.par[i] >= i || sm.tok[i] < 0 || sm.tok[i] >= V) okl = 0;
         okl = __all_sync(0xffffffffu, okl);
         if (lane == 0) {
             sm.ok = okl;
@@ -389,16 +466,17 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     if (MODE != A11S_ACCEPT_GREEDY && a.node_probs) {
         for (int r = 0; r < n_live; ++r) {
             bool has_child = false;
-            for (int c = r + 1; c < n_live && !has_child; ++c) has_child = par[c] == r;
+            for (int c = r + 1; c < n_live && !has_child; ++c) has_child = sm.par[c] == r;
             if (!has_child) continue;
             const char *prow = tgt_b + (size_t)r * row_bytes;
-            row_sums<BF16>(prow, cmax_b + (size_t)r * nch, nch, V, a.k, sm.fr, sm.sum, warp, lane);
+            row_stats_into<BF16>(prow, cmax_b + (size_t)r * nch, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr,
+                                 nch, V, a.k, sm.fr, sm.sum, warp, lane);
             __syncthreads();
             if (warp == 0) {
                 const RowStat rs = combine_sums(sm.fr, sm.sum, nch, lane);
                 for (int c = r + 1 + lane; c < n_live; c += 32) {
-                    if (par[c] != r) continue;
-                    const int x = tok[c], j = x / A11S_CHUNK;
+                    if (sm.par[c] != r) continue;
+                    const int x = sm.tok[c], j = x / A11S_CHUNK;
                     a.node_probs[(size_t)b * N + c] = prob_of(load_logit(prow, x, BF16), a.k, sm.fr[j],
                                                               chunk_scale(rs, sm.fr[j]));
                 }
@@ -417,37 +495,56 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                 int next = INT_MAX;
                 for (int c0 = node + 1; c0 < n_live && next == INT_MAX; c0 += 32) {
                     const int c = c0 + lane;
-                    const unsigned m = __ballot_sync(0xffffffffu, c < n_live && par[c] == node && tok[c] == am);
+                    const unsigned m = __ballot_sync(0xffffffffu, c < n_live && sm.par[c] == node && sm.tok[c] == am);
                     if (m) next = c0 + __ffs(m) - 1;
                 }
                 if (next == INT_MAX) { bonus = am; break; }
-                if (lane == 0) { an[alen] = next; at[alen] = tok[next]; }
+                if (lane == 0) { an[alen] = next; at[alen] = sm.tok[next]; }
                 ++alen;
                 node = next;
             }
         }
     } else {
-        // Sampling walk: warp 0 decides; every warp computes row statistics and residual passes.
+        // Sampling walk. Every warp computes a visited row's statistics (and the
+        // residual passes of DRAFT); warp 0 makes the decisions from shared memory.
         if (threadIdx.x == 0) { sm.node = 0; sm.alen = 0; }
         __syncthreads();
         for (;;) {  // one iteration per visited node
             const int nd = sm.node;
-            row_sums<BF16>(tgt_b + (size_t)nd * row_bytes, cmax_b + (size_t)nd * nch, nch, V, a.k, sm.fr, sm.sum,
-                           warp, lane);
+            const unsigned long long *rs_p = nd == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr;
+            const char *prow = tgt_b + (size_t)nd * row_bytes;
+            const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
+            row_stats_into<BF16>(prow, cmax_b + (size_t)nd * nch, rs_p, nch, V, a.k, sm.fr, sm.sum, warp, lane);
             if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                row_sums<BF16>(drf_b + (size_t)nd * row_bytes, cmax_b + (size_t)(N + nd) * nch, nch, V, a.k, sm.qfr,
-                               sm.qsum, warp, lane);
+                row_stats_into<BF16>(qrow, cmax_b + (size_t)(N + nd) * nch, nd == 0 ? rs_p + nch : nullptr, nch, V,
+                                     a.k, sm.qfr, sm.qsum, warp, lane);
             __syncthreads();
             if (warp == 0) {
                 sm.ps = combine_sums(sm.fr, sm.sum, nch, lane);
                 if (MODE == A11S_ACCEPT_STOCH_DRAFT) sm.qs = combine_sums(sm.qfr, sm.qsum, nch, lane);
                 for (int j = lane; j < nch; j += 32) sm.sub[j] = sm.sum[j];
+                // children of nd in index order, and their logits, into shared memory
+                int nk = 0;
+                for (int c0 = nd + 1; c0 < n_live; c0 += 32) {
+                    const int c = c0 + lane;
+                    const bool hit = c < n_live && sm.par[c] == nd;
+                    const unsigned m = __ballot_sync(0xffffffffu, hit);
+                    if (hit) sm.kids[nk + __popc(m & ((1u << lane) - 1u))] = c;
+                    nk += __popc(m);
+                }
+                __syncwarp();
+                for (int kk = lane; kk < nk; kk += 32) {
+                    const int x = sm.tok[sm.kids[kk]];
+                    sm.kl[kk] = load_logit(prow, x, BF16);
+                    if (MODE == A11S_ACCEPT_STOCH_DRAFT) sm.kq[kk] = load_logit(qrow, x, BF16);
+                }
                 __syncwarp();
                 if (lane == 0) {
+                    sm.nk = nk;
+                    sm.ck = 0;
                     sm.S_eff = sm.ps.S;
                     sm.nexcl = 0;
                     sm.L = 0;
-                    sm.cpos = nd;
                     sm.action = 0;
                     if (sm.ps.S == 0 || (MODE == A11S_ACCEPT_STOCH_DRAFT && sm.qs.S == 0)) {
                         report(a.status, A11S_ENONFINITE, b);
@@ -461,182 +558,202 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             __syncthreads();  // every thread has read sm.action before warp 0 rewrites it
             if (abort_walk) { failed = true; break; }
             bool moved = false;
-            for (;;) {  // children of this node, in index order
+            if (MODE == A11S_ACCEPT_STOCH_ONEHOT) {
+                // Deterministic drafts: no row passes between siblings, so warp 0
+                // tries every child without block barriers. All lanes evaluate the
+                // same shared-memory values; lane 0 writes.
                 if (warp == 0) {
-                    int next = INT_MAX;
-                    const int from = sm.cpos + 1;
-                    for (int c0 = from; c0 < n_live && next == INT_MAX; c0 += 32) {
-                        const int c = c0 + lane;
-                        const unsigned m = __ballot_sync(0xffffffffu, c < n_live && par[c] == sm.node);
-                        if (m) next = c0 + __ffs(m) - 1;
-                    }
-                    __syncwarp();
-                    if (lane == 0) {
-                        if (next == INT_MAX) {
-                            sm.action = 0;  // no child left: draw the bonus here
-                        } else {
-                            sm.cpos = next;
-                            sm.child = next;
-                            const int x = tok[next], j = x / A11S_CHUNK;
-                            const float u = a.uniforms[(size_t)b * N + next];
-                            const float lx = load_logit(tgt_b + (size_t)sm.node * row_bytes, x, BF16);
-                            if (MODE == A11S_ACCEPT_STOCH_ONEHOT) {
-                                bool ex = false;
-                                for (int e = 0; e < sm.nexcl; ++e) ex |= sm.excl[e] == x;
-                                float lt = 0.0f;
-                                if (!ex && sm.S_eff) {
-                                    RowStat re = sm.ps;
-                                    re.S = sm.S_eff;
-                                    re.invS = __ddiv_rn(1.0, __ull2double_rn(sm.S_eff));
-                                    lt = prob_of(lx, a.k, sm.fr[j], chunk_scale(re, sm.fr[j]));
-                                }
-                                if (accept_linear(u, lt, 1.0f)) {
-                                    sm.action = 1;
-                                } else {
-                                    sm.action = 2;
-                                    if (!ex) {
-                                        sm.excl[sm.nexcl++] = x;
-                                        if (sm.fr[j] != A11S_FRAME_NONE) sm.sub[j] -= det_weight(lx, a.k, (float)sm.fr[j]);
-                                        uint64_t S = 0;
-                                        for (int jj = 0; jj < nch; ++jj) {
-                                            if (sm.fr[jj] == A11S_FRAME_NONE) continue;
-                                            const int d = sm.ps.C - sm.fr[jj];
-                                            S += d > 63 ? 0ull : (sm.sub[jj] >> d);
-                                        }
-                                        sm.S_eff = S;
-                                    }
-                                }
-                            } else {
-                                const float p0 = prob_of(lx, a.k, sm.fr[j], chunk_scale(sm.ps, sm.fr[j]));
-                                const float lq = load_logit(drf_b + (size_t)sm.node * row_bytes, x, BF16);
-                                const float qx = prob_of(lq, a.k, sm.qfr[j], chunk_scale(sm.qs, sm.qfr[j]));
-                                const float lt = level_prob(p0, qx, sm.L, sm.invT);
-                                sm.action = accept_linear(u, lt, qx) ? 1 : (sm.L < A11S_MAX_WALK_LEVELS ? 4 : 2);
+                    int next = -1;
+                    for (int kk = 0; kk < sm.nk; ++kk) {
+                        const int c = sm.kids[kk], x = sm.tok[c], j = x / A11S_CHUNK;
+                        bool ex = false;
+                        for (int e = 0; e < sm.nexcl; ++e) ex |= sm.excl[e] == x;
+                        float lt = 0.0f;
+                        const uint64_t S_eff = sm.S_eff;
+                        if (!ex && S_eff) {
+                            RowStat re = sm.ps;
+                            re.S = S_eff;
+                            re.invS = __ddiv_rn(1.0, __ull2double_rn(S_eff));
+                            lt = prob_of(sm.kl[kk], a.k, sm.fr[j], chunk_scale(re, sm.fr[j]));
+                        }
+                        if (accept_linear(sm.uni[c], lt, 1.0f)) { next = c; break; }
+                        if (!ex) {
+                            __syncwarp();
+                            if (lane == 0) {
+                                sm.excl[sm.nexcl++] = x;
+                                if (sm.fr[j] != A11S_FRAME_NONE) sm.sub[j] -= det_weight(sm.kl[kk], a.k, (float)sm.fr[j]);
                             }
+                            __syncwarp();
+                            uint64_t S = 0;  // warp-parallel renormalisation
+                            for (int jj = lane; jj < nch; jj += 32) {
+                                if (sm.fr[jj] == A11S_FRAME_NONE) continue;
+                                const int d = sm.ps.C - sm.fr[jj];
+                                S += d > 63 ? 0ull : (sm.sub[jj] >> d);
+                            }
+                            S = warp_sum_u64(S);
+                            if (lane == 0) sm.S_eff = S;
+                            __syncwarp();
                         }
                     }
+                    if (lane == 0 && next >= 0) {
+                        an[sm.alen] = next;
+                        at[sm.alen] = sm.tok[next];
+                        sm.alen += 1;
+                        sm.node = next;
+                    }
+                    if (lane == 0) sm.child = next;
                     __syncwarp();
                 }
                 __syncthreads();
-                const int action = sm.action;
-                __syncthreads();  // every thread has read sm.action before it changes
-                if (action == 1) {  // accepted: move to the child
-                    if (threadIdx.x == 0) {
-                        an[sm.alen] = sm.child;
-                        at[sm.alen] = tok[sm.child];
-                        sm.alen += 1;
-                        sm.node = sm.child;
+                moved = sm.child >= 0;
+                __syncthreads();
+            } else {
+                for (;;) {  // children of this node, in index order
+                    if (warp == 0 && lane == 0) {
+                        if (sm.ck >= sm.nk) {
+                            sm.action = 0;  // no child left: draw the bonus here
+                        } else {
+                            const int kk = sm.ck++;
+                            const int c = sm.kids[kk], x = sm.tok[c], j = x / A11S_CHUNK;
+                            sm.child = c;
+                            const float p0 = prob_of(sm.kl[kk], a.k, sm.fr[j], chunk_scale(sm.ps, sm.fr[j]));
+                            const float qx = prob_of(sm.kq[kk], a.k, sm.qfr[j], chunk_scale(sm.qs, sm.qfr[j]));
+                            const float lt = level_prob(p0, qx, sm.L, sm.invT);
+                            sm.action = accept_linear(sm.uni[c], lt, qx) ? 1 : (sm.L < A11S_MAX_WALK_LEVELS ? 4 : 2);
+                        }
                     }
-                    moved = true;
                     __syncthreads();
-                    break;
-                }
-                if (action == 0) break;
-                if (action == 4) {
-                    // DRAFT residual pass: chunk totals of level L+1 (every warp).
-                    const char *prow = tgt_b + (size_t)sm.node * row_bytes;
-                    const char *qrow = drf_b + (size_t)sm.node * row_bytes;
-                    const int L = sm.L;
-                    constexpr int EPV = Vec<BF16>::EPV, NV = Vec<BF16>::NV, G = 4;
-                    for (int j = warp; j < nch; j += kWarps) {
-                        const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-                        const int32_t fp = sm.fr[j], fq = sm.qfr[j];
-                        const double scp = chunk_scale(sm.ps, fp), scq = chunk_scale(sm.qs, fq);
-                        uint64_t s = 0;
-                        for (int i0 = 0; i0 < NV; i0 += G) {  // 4 vectors of p and q in flight
-                            uint4 vp[G], vq[G];
+                    const int action = sm.action;
+                    __syncthreads();  // every thread has read sm.action before it changes
+                    if (action == 1) {  // accepted: move to the child
+                        if (threadIdx.x == 0) {
+                            an[sm.alen] = sm.child;
+                            at[sm.alen] = sm.tok[sm.child];
+                            sm.alen += 1;
+                            sm.node = sm.child;
+                        }
+                        moved = true;
+                        __syncthreads();
+                        break;
+                    }
+                    if (action == 0) break;
+                    if (action == 4) {
+                        // DRAFT residual pass: chunk totals of level L+1 (every warp).
+                        const int L = sm.L;
+                        constexpr int EPV = Vec<BF16>::EPV, NV = Vec<BF16>::NV, G = 4;
+                        for (int j = warp; j < nch; j += kWarps) {
+                            const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+                            const int32_t fp = sm.fr[j], fq = sm.qfr[j];
+                            const double scp = chunk_scale(sm.ps, fp), scq = chunk_scale(sm.qs, fq);
+                            uint64_t s = 0;
+                            for (int i0 = 0; i0 < NV; i0 += G) {  // 4 vectors of p and q in flight
+                                uint4 vp[G], vq[G];
 #pragma unroll
-                            for (int g = 0; g < G; ++g) {
-                                const int e0 = ((i0 + g) * 32 + lane) * EPV;
-                                const size_t off = (size_t)(c0 + e0) * (BF16 ? 2 : 4);
-                                const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
-                                vp[g] = e0 < clen ? ldg_stream(prow + off) : make_uint4(ninf, ninf, ninf, ninf);
-                                vq[g] = e0 < clen ? ldg_stream(qrow + off) : make_uint4(ninf, ninf, ninf, ninf);
-                            }
-#pragma unroll
-                            for (int g = 0; g < G; ++g)
-#pragma unroll
-                                for (int e = 0; e < EPV; ++e) {
-                                    const float pv = prob_of(Vec<BF16>::at(vp[g], e), a.k, fp, scp);
-                                    const float qv = prob_of(Vec<BF16>::at(vq[g], e), a.k, fq, scq);
-                                    s += level_weight(level_prob(pv, qv, L, sm.invT), qv);
+                                for (int g = 0; g < G; ++g) {
+                                    const int e0 = ((i0 + g) * 32 + lane) * EPV;
+                                    const size_t off = (size_t)(c0 + e0) * (BF16 ? 2 : 4);
+                                    const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+                                    vp[g] = e0 < clen ? ldg_stream(prow + off) : make_uint4(ninf, ninf, ninf, ninf);
+                                    vq[g] = e0 < clen ? ldg_stream(qrow + off) : make_uint4(ninf, ninf, ninf, ninf);
                                 }
+#pragma unroll
+                                for (int g = 0; g < G; ++g)
+#pragma unroll
+                                    for (int e = 0; e < EPV; ++e) {
+                                        const float pv = prob_of(Vec<BF16>::at(vp[g], e), a.k, fp, scp);
+                                        const float qv = prob_of(Vec<BF16>::at(vq[g], e), a.k, fq, scq);
+                                        s += level_weight(level_prob(pv, qv, L, sm.invT), qv);
+                                    }
+                            }
+                            s = warp_sum_u64(s);
+                            if (lane == 0) sm.tmp[j] = s;
                         }
-                        s = warp_sum_u64(s);
-                        if (lane == 0) sm.tmp[j] = s;
-                    }
-                    __syncthreads();
-                    if (threadIdx.x == 0) {
-                        uint64_t tot = 0;
-                        for (int j = 0; j < nch; ++j) tot += sm.tmp[j];
-                        if (tot) {
-                            sm.L += 1;
-                            sm.T[sm.L] = tot;
-                            sm.invT[sm.L] = __ddiv_rn(1.0, __ull2double_rn(tot));
-                            for (int j = 0; j < nch; ++j) sm.lvl[j] = sm.tmp[j];
+                        __syncthreads();
+                        if (warp == 0) {
+                            uint64_t tot = 0;
+                            for (int j = lane; j < nch; j += 32) tot += sm.tmp[j];
+                            tot = warp_sum_u64(tot);
+                            if (tot) {
+                                for (int j = lane; j < nch; j += 32) sm.lvl[j] = sm.tmp[j];
+                                if (lane == 0) {
+                                    sm.L += 1;
+                                    sm.T[sm.L] = tot;
+                                    sm.invT[sm.L] = __ddiv_rn(1.0, __ull2double_rn(tot));
+                                }
+                            }
                         }
+                        __syncthreads();
                     }
-                    __syncthreads();
+                    // action 2 / 4: rejected, try the next child
                 }
-                // action 2 / 4: rejected, try the next child
             }
             if (!moved) break;
         }
-        // bonus draw at sm.node (warp 0)
-        if (!failed && warp == 0) {
+        // bonus draw at sm.node: warp 0 picks the chunk, every thread scans it
+        if (!failed) {
             const int nd = sm.node;
             const char *prow = tgt_b + (size_t)nd * row_bytes;
-            const float u0 = a.uniforms[(size_t)b * N];
-            int j = 0;
-            uint64_t t2 = 0;
-            bool okp = false;
-            if (MODE == A11S_ACCEPT_STOCH_DRAFT && sm.L > 0) {
-                if (lane == 0) okp = pick_chunk(u0, sm.lvl, sm.lvl, nch, j, t2);
-                okp = __shfl_sync(0xffffffffu, okp, 0);
-                j = __shfl_sync(0xffffffffu, j, 0);
-                t2 = __shfl_sync(0xffffffffu, t2, 0);
-                if (okp) {
-                    const char *qrow = drf_b + (size_t)nd * row_bytes;
+            const bool draft_lvl = MODE == A11S_ACCEPT_STOCH_DRAFT && sm.L > 0;
+            const bool use_excl = MODE == A11S_ACCEPT_STOCH_ONEHOT && sm.S_eff != 0;
+            if (warp == 0) {
+                int j = 0;
+                uint64_t t2 = 0;
+                bool okp;
+                if (draft_lvl) {
+                    okp = pick_chunk(sm.uni[0], sm.lvl, sm.lvl, nch, lane, j, t2);
+                } else {
+                    // A_j in the row frame, local totals Lc_j (sm.tmp / sm.lvl as scratch)
+                    for (int jj = lane; jj < nch; jj += 32) {
+                        const uint64_t loc = use_excl ? sm.sub[jj] : sm.sum[jj];
+                        sm.tmp[jj] = loc;
+                        const int32_t f = sm.fr[jj];
+                        const int d = sm.ps.C - f;
+                        sm.lvl[jj] = (f == A11S_FRAME_NONE || d > 63) ? 0ull : (loc >> d);
+                    }
+                    __syncwarp();
+                    okp = pick_chunk(sm.uni[0], sm.lvl, sm.tmp, nch, lane, j, t2);
+                }
+                if (lane == 0) {
+                    sm.bj = okp ? j : -1;
+                    sm.bt2 = t2;
+                }
+            }
+            __syncthreads();
+            const int j = sm.bj;
+            const uint64_t t2 = sm.bt2;
+            if (j >= 0) {
+                const float k = a.k;
+                const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+                const char *pc = prow + (size_t)c0 * (BF16 ? 2 : 4);
+                int pos;
+                if (draft_lvl) {
+                    const char *qc = drf_b + (size_t)nd * row_bytes + (size_t)c0 * (BF16 ? 2 : 4);
                     const int32_t fp = sm.fr[j], fq = sm.qfr[j];
                     const double scp = chunk_scale(sm.ps, fp), scq = chunk_scale(sm.qs, fq);
                     const int L = sm.L;
-                    const float k = a.k;
-                    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-                    stage_chunk<BF16>(prow, c0, clen, sm.cp, lane);
-                    stage_chunk<BF16>(qrow, c0, clen, sm.cq, lane);
-                    bonus = c0 + scan_chunk(clen, t2, lane, [&](int e) {
-                                const float pv = prob_of(sm.cp[e], k, fp, scp);
-                                const float qv = prob_of(sm.cq[e], k, fq, scq);
-                                return level_weight(level_prob(pv, qv, L - 1, sm.invT), qv);
-                            });
-                }
-            } else {
-                const bool use_excl = MODE == A11S_ACCEPT_STOCH_ONEHOT && sm.S_eff != 0;
-                // A_j in the row frame, local totals Lc_j (sm.tmp / sm.lvl as scratch)
-                for (int jj = lane; jj < nch; jj += 32) {
-                    const uint64_t loc = use_excl ? sm.sub[jj] : sm.sum[jj];
-                    sm.tmp[jj] = loc;
-                    const int32_t f = sm.fr[jj];
-                    const int d = sm.ps.C - f;
-                    sm.lvl[jj] = (f == A11S_FRAME_NONE || d > 63) ? 0ull : (loc >> d);
-                }
-                __syncwarp();
-                if (lane == 0) okp = pick_chunk(u0, sm.lvl, sm.tmp, nch, j, t2);
-                okp = __shfl_sync(0xffffffffu, okp, 0);
-                j = __shfl_sync(0xffffffffu, j, 0);
-                t2 = __shfl_sync(0xffffffffu, t2, 0);
-                if (okp) {
+                    pos = block_scan_chunk(clen, t2, [&](int p0, uint64_t *w) {
+                        float pv[4], qv[4];
+                        load4<BF16>(pc, p0, pv);
+                        load4<BF16>(qc, p0, qv);
+                        for (int e = 0; e < 4; ++e) {
+                            const float pp = prob_of(pv[e], k, fp, scp), qq = prob_of(qv[e], k, fq, scq);
+                            w[e] = level_weight(level_prob(pp, qq, L - 1, sm.invT), qq);
+                        }
+                    }, sm);
+                } else {
                     const float cff = (float)sm.fr[j];
-                    const float k = a.k;
                     const int nex = use_excl ? sm.nexcl : 0;
-                    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-                    stage_chunk<BF16>(prow, c0, clen, sm.cp, lane);
-                    bonus = c0 + scan_chunk(clen, t2, lane, [&](int e) -> uint64_t {
-                                for (int x = 0; x < nex; ++x)
-                                    if (sm.excl[x] == c0 + e) return 0ull;
-                                return det_weight(sm.cp[e], k, cff);
-                            });
+                    pos = block_scan_chunk(clen, t2, [&](int p0, uint64_t *w) {
+                        float l[4];
+                        load4<BF16>(pc, p0, l);
+                        for (int e = 0; e < 4; ++e) {
+                            bool ex = false;
+                            for (int x = 0; x < nex; ++x) ex |= sm.excl[x] == c0 + p0 + e;
+                            w[e] = ex ? 0ull : det_weight(l[e], k, cff);
+                        }
+                    }, sm);
                 }
+                bonus = c0 + pos;
             }
             alen = sm.alen;
         }

@@ -49,7 +49,7 @@ int sm_count() {
 
 // ---- acceptance workspace layout ----
 struct AcceptLayout {
-    size_t counters, recs, total;
+    size_t counters, recs, root_sums, total;
 };
 AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
     AcceptLayout L;
@@ -57,7 +57,8 @@ AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32
     const size_t rows = (size_t)batch * max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
     L.counters = kHeaderBytes;
     L.recs = L.counters + up256(sizeof(int32_t) * (size_t)batch);
-    L.total = L.recs + up256(rows * nch * sizeof(float));
+    L.root_sums = L.recs + up256(rows * nch * sizeof(float));
+    L.total = L.root_sums + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * 2 * nch * sizeof(uint64_t)));
     return L;
 }
 
@@ -103,9 +104,9 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     if (dtype != A11S_F32 && dtype != A11S_BF16)
         return fail(A11S_EINVAL, "a11s_accept: unknown dtype %d", dtype);
     if (batch < 0) return fail(A11S_EINVAL, "a11s_accept: batch %d < 0", batch);
-    if (max_nodes < 1 || max_nodes > A11S_MAX_NODES)
+    if (max_nodes < 1 || max_nodes > A11S_MAX_ACCEPT_NODES)
         return fail(A11S_EUNSUPPORTED, "a11s_accept: max_nodes %d outside [1, %d]", max_nodes,
-                    A11S_MAX_NODES);
+                    A11S_MAX_ACCEPT_NODES);
     if (vocab < 1 || vocab > A11S_MAX_VOCAB)
         return fail(A11S_EUNSUPPORTED, "a11s_accept: vocab %d outside [1, %d]", vocab, A11S_MAX_VOCAB);
     const int vec = dtype == A11S_BF16 ? 8 : 4;
@@ -157,6 +158,7 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.status = reinterpret_cast<a11s::StatusWord *>(ws);
     a.counters = reinterpret_cast<int32_t *>(ws + L.counters);
     a.recs = reinterpret_cast<float *>(ws + L.recs);
+    a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
 
     // Balance: about 4 waves of 2 resident 512-thread blocks per SM, at least
     // 16 chunks (one per warp) per block.

@@ -9,8 +9,9 @@
 #define A11S_CHUNK 2048           // tokens per softmax chunk (fixed by the numeric contract)
 #define A11S_FRAME_NONE INT32_MIN // chunk whose logits are all -inf
 #define A11S_MAX_WALK_LEVELS 64   // residual levels kept per node (STOCH_DRAFT)
-#define A11S_MAX_VOCAB (1 << 20)  // keeps every uint64 weight sum below 2^63
-#define A11S_MAX_NODES 1024
+#define A11S_MAX_VOCAB (1 << 18)  // 262144 tokens: 128 chunks; weight sums stay far below 2^63
+#define A11S_MAX_NODES 1024        // tree size limit of the n-gram expansion
+#define A11S_MAX_ACCEPT_NODES 256  // tree size limit of the acceptance kernel (staged in shared memory)
 
 namespace a11s {
 

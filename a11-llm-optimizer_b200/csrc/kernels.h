@@ -24,6 +24,7 @@ struct AcceptArgs {
     float *node_probs;
     long long *stats;
     float *recs;  // [B][rows_per_seq][nch] chunk maxima (NaN-propagating)
+    unsigned long long *root_sums;  // [B][2][nch] weight sums of the root rows (p, q)
     int32_t *counters;
     StatusWord *status;
 };

@@ -122,7 +122,8 @@ int a11s_read_status(const void *workspace, int32_t *status, int32_t *detail, vo
  *   = p(tokens[i]) in the parent's row before any residual, 0 for the root.
  * Rows are `row_stride` elements apart (>= vocab; multiple of 8 for bf16 and
  * of 4 for fp32; 16-byte aligned base pointers). draft_logits is used only by
- * STOCH_DRAFT and has the same layout as target_logits.
+ * STOCH_DRAFT and has the same layout as target_logits. Implemented sizes:
+ * vocab <= 262144, max_nodes <= 256 (A11S_EUNSUPPORTED beyond).
  */
 size_t a11s_accept_workspace_bytes(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab);
 
