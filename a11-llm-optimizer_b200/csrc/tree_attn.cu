@@ -17,9 +17,13 @@
 //   warp 9     TMEM allocator + single-thread MMA issuer
 // Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N64 K16 into TMEM,
 // two S buffers per tile), softmax warps mask (ancestor bits), exponentiate
-// with one FFMA + ex2 per score, pack P_j to bf16 with integer ops and write
-// it to shared memory in the canonical 128-byte-swizzled K-major layout, then
-// O += P_j V_j (4 MMAs M128 N128 K16, V as an MN-major operand) in TMEM.
+// with one FFMA + ex2 per score, pack P_j to bf16 with integer ops and store
+// it into the first 32 columns of its own S buffer in TMEM, then
+// O += P_j V_j (4 MMAs M128 N128 K16 with A = P read from TMEM and V an
+// MN-major shared-memory operand). Keeping P in TMEM leaves the tensor core's
+// shared-memory port (about 128 B/clk) to Q, K and V: an M128 N64 K16 MMA with
+// both operands in shared memory is bound by that port, not by its math.
+// An S buffer is reused by QK(j+2) only after PV(j) of its tile completed.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
 // exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
@@ -39,7 +43,7 @@ namespace a11s {
 namespace {
 constexpr int kBlockKV = 64;          // keys per KV block = 4 pages
 constexpr int kPagesPerBlock = kBlockKV / A11S_PAGE_TOKENS;
-constexpr int kStages = 3;            // K+V ring depth (each stage serves both Q tiles)
+constexpr int kStages = 4;            // K+V ring depth (each stage serves both Q tiles)
 constexpr int kTiles = 2;             // Q tiles per CTA, 128 rows each
 constexpr int kNodesPerTile = 16;
 constexpr int kNodesPerCta = kTiles * kNodesPerTile;
@@ -51,11 +55,9 @@ constexpr uint32_t kKVHalf = 8192;    // K or V: 64 tokens x 128 B per 64-dim ha
 constexpr uint32_t kOffQ = 0;                                // tile t at 2*kQHalf*t
 constexpr uint32_t kOffKV = kTiles * 2 * kQHalf;             // stage s: K at +0, V at +16 KB
 constexpr uint32_t kStageBytes = 4 * kKVHalf;                // 32 KB
-constexpr uint32_t kOffP = kOffKV + kStages * kStageBytes;   // [tile][buffer] x 16 KB
-constexpr uint32_t kPBytes = 16384;
-constexpr uint32_t kOffBar = kOffP + kTiles * 2 * kPBytes;   // 229376
+constexpr uint32_t kOffBar = kOffKV + kStages * kStageBytes;
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-constexpr uint32_t kTmemCols = 512;   // S [tile][buffer] at 128 t + 64 b, O[tile] at 256 + 128 t
+constexpr uint32_t kTmemCols = 512;   // S/P [tile][buffer] at 128 t + 64 b, O[tile] at 256 + 128 t
 constexpr uint32_t kColO = 256;
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
@@ -65,7 +67,7 @@ constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 struct Bars {
     uint64_t q_full;
     uint64_t kv_full[kStages], kv_empty[kStages];
-    uint64_t s_full[kTiles][2], s_free[kTiles][2], p_full[kTiles][2], p_free[kTiles][2];
+    uint64_t s_full[kTiles][2], p_full[kTiles][2], p_free[kTiles][2];
     uint64_t drain;
     uint32_t tmem_base;
     int32_t abort;
@@ -179,7 +181,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int t = 0; t < kTiles; ++t)
             for (int s = 0; s < 2; ++s) {
                 tc::mbar_init(&bs->s_full[t][s], 1);
-                tc::mbar_init(&bs->s_free[t][s], 128);
                 tc::mbar_init(&bs->p_full[t][s], 128);
                 tc::mbar_init(&bs->p_free[t][s], 1);
             }
@@ -278,44 +279,53 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            auto issue_s = [&](int it) -> bool {
+            auto issue_s = [&](int it, int t) {  // S(it) of tile t into S buffer it & 1
                 const int sb = it & 1, st = it % kStages;
-                if (!wait_or_abort(&bs->kv_full[st], (it / kStages) & 1, bs, p.status)) return false;
                 const uint32_t k_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes);
-                for (int t = 0; t < kTiles; ++t) {
-                    if (it >= 2 && !wait_or_abort(&bs->s_free[t][sb], ((it >> 1) - 1) & 1, bs, p.status)) return false;
-                    tc::tc_fence_after();
-                    const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
+                const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
 #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-                        const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                        tc::mma_bf16_ss(tmem + t * 128 + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
-                                        tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
-                    }
-                    tc::mma_commit(&bs->s_full[t][sb]);
+                for (int kk = 0; kk < 8; ++kk) {
+                    const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+                    const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+                    tc::mma_bf16_ss(tmem + t * 128 + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
+                                    tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
                 }
-                return true;
+                tc::mma_commit(&bs->s_full[t][sb]);
             };
             bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
-            ok = ok && issue_s(0);
+            for (int it = 0; it < min(nb, 2) && ok; ++it) {
+                ok = wait_or_abort(&bs->kv_full[it % kStages], (it / kStages) & 1, bs, p.status);
+                if (!ok) break;
+                tc::tc_fence_after();
+                for (int t = 0; t < kTiles; ++t) issue_s(it, t);
+            }
             for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
-                if (it + 1 < nb && !issue_s(it + 1)) break;
                 const int pb = it & 1, st = it % kStages;
                 const uint32_t v_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes + 2 * kKVHalf);
                 for (int t = 0; t < kTiles && ok; ++t) {
                     if (!wait_or_abort(&bs->p_full[t][pb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
                     tc::tc_fence_after();
-                    const uint32_t p_addr = tc::smem_u32(sm + kOffP + (t * 2 + pb) * kPBytes);
+                    const uint32_t p_tmem = tmem + t * 128 + pb * kBlockKV;
 #pragma unroll
                     for (int kk = 0; kk < kBlockKV / 16; ++kk) {
-                        tc::mma_bf16_ss(tmem + kColO + t * 128, tc::sdesc_sw128(p_addr + kk * 32, 16, 1024),
+                        tc::mma_bf16_ts(tmem + kColO + t * 128, p_tmem + kk * 8,
                                         tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
                                         (it > 0 || kk > 0) ? 1u : 0u);
                     }
                     tc::mma_commit(&bs->p_free[t][pb]);
                 }
+                if (!ok) break;
                 tc::mma_commit(&bs->kv_empty[st]);
+                const int in = it + 2;  // S(it + 2) reuses the buffer that holds P(it)
+                if (in < nb) {
+                    if (!wait_or_abort(&bs->kv_full[in % kStages], (in / kStages) & 1, bs, p.status)) { ok = false; break; }
+                    for (int t = 0; t < kTiles && ok; ++t) {
+                        // PV(it) of tile t has read P(it) from the buffer (this overlaps PV(it) of the next tile)
+                        if (!wait_or_abort(&bs->p_free[t][pb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+                        tc::tc_fence_after();
+                        issue_s(in, t);
+                    }
+                }
             }
             // wait for every issued MMA before the CTA may release TMEM
             tc::mma_commit(&bs->drain);
@@ -338,8 +348,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             tc::tc_fence_after();
             float x[kBlockKV];
             tc::tmem_ld64(tmem + lane_base + col_s + sb * kBlockKV, x);
-            tc::tc_fence_before();
-            tc::mbar_arrive(&bs->s_free[tile][sb]);
             // mask (raw scores) and block max
             if (live && p0 + kBlockKV > L) {
 #pragma unroll
@@ -383,27 +391,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             lsum *= alpha;
-            // P buffer sb is free once PV(it-2) completed
-            if (it >= 2 && !wait_or_abort(&bs->p_free[tile][sb], ((it >> 1) - 1) & 1, bs, p.status)) { ok = false; break; }
             const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
-            uint8_t *prow = sm + kOffP + (tile * 2 + sb) * kPBytes + (m >> 3) * 1024 + (m & 7) * 128;
+            uint32_t pw[kBlockKV / 2];  // P row as bf16 pairs, lower key in the low half
             float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
 #pragma unroll
-            for (int c = 0; c < 8; ++c) {
-                uint32_t w[4];
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const int col = c * 8 + 2 * e;
-                    const float a0 = tc::ex2(fmaf(x[col], sl2, neg));
-                    const float a1 = tc::ex2(fmaf(x[col + 1], sl2, neg));
-                    w[e] = pack_bf16x2(a0, a1);
-                    ls[(2 * e) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
-                    ls[(2 * e + 1) & 7] += a1;
-                }
-                *reinterpret_cast<uint4 *>(prow + ((c ^ (m & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+            for (int c = 0; c < kBlockKV / 2; ++c) {
+                const float a0 = tc::ex2(fmaf(x[2 * c], sl2, neg));
+                const float a1 = tc::ex2(fmaf(x[2 * c + 1], sl2, neg));
+                pw[c] = pack_bf16x2(a0, a1);
+                ls[(2 * c) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
+                ls[(2 * c + 1) & 7] += a1;
             }
             lsum += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-            tc::fence_proxy_async_smem();
+            // P over the first 32 columns of this S buffer (S is already in registers)
+            tc::tmem_st32u(tmem + lane_base + col_s + sb * kBlockKV, pw);
             tc::tc_fence_before();
             tc::mbar_arrive(&bs->p_full[tile][sb]);
         }
