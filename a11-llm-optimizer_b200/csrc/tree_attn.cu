@@ -9,21 +9,23 @@
 //
 // One CTA = one sequence b, one KV head g, 32 tree nodes x 8 query heads as
 // two Q tiles of 128 rows (the MMA M), one split of the KV range. 320 threads:
-//   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane;
-//              two softmax warps per scheduler hide each other's latency
-//   warp 8     TMA producer: Q once, then K and V blocks of 64 keys (4 pages,
-//              one 64x16 box per page and 64-column half) into a 3-stage ring
-//              shared by both tiles; page ids fetched 8 blocks ahead
+//   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane
+//   warp 8     TMA producer: Q once, then K and V blocks of 128 keys (8 pages,
+//              one 64x16 box per page and 64-column half) into a 3-slot K
+//              ring and a 2-slot V ring shared by both tiles (a K slot frees
+//              after QK^T, long before PV); page ids fetched 4 blocks ahead
 //   warp 9     TMEM allocator + single-thread MMA issuer
-// Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N64 K16 into TMEM,
-// two S buffers per tile), softmax warps mask (ancestor bits), exponentiate
-// with one FFMA + ex2 per score, pack P_j to bf16 with integer ops and store
-// it into the first 32 columns of its own S buffer in TMEM, then
-// O += P_j V_j (4 MMAs M128 N128 K16 with A = P read from TMEM and V an
-// MN-major shared-memory operand). Keeping P in TMEM leaves the tensor core's
-// shared-memory port (about 128 B/clk) to Q, K and V: an M128 N64 K16 MMA with
-// both operands in shared memory is bound by that port, not by its math.
-// An S buffer is reused by QK(j+2) only after PV(j) of its tile completed.
+// TMEM (512 columns): per tile one S/P buffer of 128 columns and O (128 dims).
+// Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N128 K16), the
+// softmax warps mask it (ancestor bits), exponentiate with one FFMA + ex2 per
+// score, pack P_j to bf16 with integer ops and store it over the first 64
+// columns of the same buffer, then O += P_j V_j (8 MMAs M128 N128 K16, A = P
+// read from TMEM, V an MN-major shared-memory operand). S_{j+1} of a tile is
+// issued once PV_j of that tile has completed (S and P share columns); the
+// two tiles alternate, so one tile's softmax overlaps the other's MMAs.
+// Why this shape: an M128 N64 K16 MMA costs about 58 cycles whatever its
+// operands, against 32 of math, while N = 128 runs at its math rate; and P in
+// TMEM keeps the tensor core's shared-memory port (about 128 B/clk) for Q, K, V.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
 // exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
@@ -41,9 +43,10 @@
 namespace a11s {
 
 namespace {
-constexpr int kBlockKV = 64;          // keys per KV block = 4 pages
+constexpr int kBlockKV = 128;         // keys per KV block = 8 pages (the N of the QK^T MMA)
 constexpr int kPagesPerBlock = kBlockKV / A11S_PAGE_TOKENS;
-constexpr int kStages = 4;            // K+V ring depth (each stage serves both Q tiles)
+constexpr int kKStages = 3;           // K ring depth: a K slot is free once QK^T of both tiles completed
+constexpr int kVStages = 2;           // V ring depth: a V slot is free once PV of both tiles completed
 constexpr int kTiles = 2;             // Q tiles per CTA, 128 rows each
 constexpr int kNodesPerTile = 16;
 constexpr int kNodesPerCta = kTiles * kNodesPerTile;
@@ -51,13 +54,14 @@ constexpr int kSoftmaxWarps = 4 * kTiles;
 constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
 constexpr int kTcThreads = 32 * (kSoftmaxWarps + 2);
 constexpr uint32_t kQHalf = 16384;    // Q tile: 128 rows x 128 B per 64-dim half
-constexpr uint32_t kKVHalf = 8192;    // K or V: 64 tokens x 128 B per 64-dim half
+constexpr uint32_t kKVHalf = 16384;   // K or V: 128 tokens x 128 B per 64-dim half
 constexpr uint32_t kOffQ = 0;                                // tile t at 2*kQHalf*t
-constexpr uint32_t kOffKV = kTiles * 2 * kQHalf;             // stage s: K at +0, V at +16 KB
-constexpr uint32_t kStageBytes = 4 * kKVHalf;                // 32 KB
-constexpr uint32_t kOffBar = kOffKV + kStages * kStageBytes;
+constexpr uint32_t kSlotBytes = 2 * kKVHalf;                 // one K or V block: 32 KB
+constexpr uint32_t kOffK = kTiles * 2 * kQHalf;              // K slots
+constexpr uint32_t kOffV = kOffK + kKStages * kSlotBytes;    // V slots
+constexpr uint32_t kOffBar = kOffV + kVStages * kSlotBytes;  // 229376
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-constexpr uint32_t kTmemCols = 512;   // S/P [tile][buffer] at 128 t + 64 b, O[tile] at 256 + 128 t
+constexpr uint32_t kTmemCols = 512;   // S/P[tile] at 128 t (P over its first 64 columns), O[tile] at 256 + 128 t
 constexpr uint32_t kColO = 256;
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
@@ -66,8 +70,8 @@ constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 
 struct Bars {
     uint64_t q_full;
-    uint64_t kv_full[kStages], kv_empty[kStages];
-    uint64_t s_full[kTiles][2], p_full[kTiles][2], p_free[kTiles][2];
+    uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
+    uint64_t s_full[kTiles], p_full[kTiles], p_free[kTiles];
     uint64_t drain;
     uint32_t tmem_base;
     int32_t abort;
@@ -100,9 +104,9 @@ int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t
     double best_cost = 1e300;
     for (int s = 1; s <= 32; ++s) {
         const int bps = (blocks + s - 1) / s;
-        if (s > 1 && bps < 16) break;
+        if (s > 1 && bps < 8) break;
         const long long waves = (ctas * s + sms - 1) / sms;
-        const double cost = (double)waves * (bps + 8.0);  // ~8 blocks of fixed per-CTA cost
+        const double cost = (double)waves * (bps + 4.0);  // ~4 blocks of fixed per-CTA cost
         if (cost < best_cost * 0.98) { best_cost = cost; best = s; }
     }
     return best;
@@ -174,16 +178,19 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // ---------------- setup ----------------
     if (tid == 0) {
         tc::mbar_init(&bs->q_full, 1);
-        for (int s = 0; s < kStages; ++s) {
-            tc::mbar_init(&bs->kv_full[s], 1);
-            tc::mbar_init(&bs->kv_empty[s], 1);
+        for (int s = 0; s < kKStages; ++s) {
+            tc::mbar_init(&bs->k_full[s], 1);
+            tc::mbar_init(&bs->k_empty[s], 1);
         }
-        for (int t = 0; t < kTiles; ++t)
-            for (int s = 0; s < 2; ++s) {
-                tc::mbar_init(&bs->s_full[t][s], 1);
-                tc::mbar_init(&bs->p_full[t][s], 128);
-                tc::mbar_init(&bs->p_free[t][s], 1);
-            }
+        for (int s = 0; s < kVStages; ++s) {
+            tc::mbar_init(&bs->v_full[s], 1);
+            tc::mbar_init(&bs->v_empty[s], 1);
+        }
+        for (int t = 0; t < kTiles; ++t) {
+            tc::mbar_init(&bs->s_full[t], 1);
+            tc::mbar_init(&bs->p_full[t], 128);
+            tc::mbar_init(&bs->p_free[t], 1);
+        }
         tc::mbar_init(&bs->drain, 1);
         bs->abort = 0;
         tc::fence_barrier_init();
@@ -233,8 +240,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
             }
         }
-        // Page ids of 8 blocks (32 entries) per coalesced warp load, double
-        // buffered, so a block's ids were requested 8 blocks before use.
+        // Page ids of 4 blocks (32 entries) per coalesced warp load, double
+        // buffered, so a block's ids were requested 4 blocks before use.
+        constexpr int kBlocksPerWindow = 32 / kPagesPerBlock;
         const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
         const int lp0 = blk0 * kPagesPerBlock;
         const int lp_end = min((kv_len + A11S_PAGE_TOKENS - 1) / A11S_PAGE_TOKENS, (blk0 + nb) * kPagesPerBlock);
@@ -244,11 +252,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             return lp < p.max_pages ? __ldg(pt + lp) : -1;
         };
         int cur = window(0), nxt = window(1);
+        int nk = 0, nv = 0;  // K and V blocks whose loads were issued
         for (int it = 0; it < nb && !aborted(bs); ++it) {
-            const int s = it % kStages, use = it / kStages, k = it & 7;
+            const int k = it % kBlocksPerWindow;
             if (k == 0 && it > 0) {
                 cur = nxt;
-                nxt = window((it >> 3) + 1);
+                nxt = window(it / kBlocksPerWindow + 1);
             }
             const int id = __shfl_sync(0xffffffffu, cur, (k * kPagesPerBlock + lane) & 31);
             int page = p.num_pages;  // out of range -> zero fill
@@ -256,74 +265,88 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
                 else page = id;
             }
-            if (lane == 0 && use > 0) wait_or_abort(&bs->kv_empty[s], (use - 1) & 1, bs, p.status);
+            // K(it): its slot was last read by QK(it - kKStages)
+            const int ks = it % kKStages, kuse = it / kKStages;
+            if (lane == 0 && kuse > 0) wait_or_abort(&bs->k_empty[ks], (kuse - 1) & 1, bs, p.status);
             __syncwarp();
             if (aborted(bs)) break;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->kv_full[s], kStageBytes);
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->k_full[ks], kSlotBytes);
             __syncwarp();
-            uint8_t *sK = sm + kOffKV + s * kStageBytes;
-            uint8_t *sV = sK + 2 * kKVHalf;
+            uint8_t *sK = sm + kOffK + ks * kSlotBytes;
             if (lane < kPagesPerBlock) {
-                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->kv_full[s], 0, g, 0, page);
-                tc::tma_load_4d(sK + kKVHalf + lane * 2048, &tk, &bs->kv_full[s], 64, g, 0, page);
-                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->kv_full[s], 0, g, 0, page);
-                tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->kv_full[s], 64, g, 0, page);
+                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->k_full[ks], 0, g, 0, page);
+                tc::tma_load_4d(sK + kKVHalf + lane * 2048, &tk, &bs->k_full[ks], 64, g, 0, page);
             }
+            ++nk;
+            // V(it): its slot was last read by PV(it - kVStages)
+            const int vs = it % kVStages, vuse = it / kVStages;
+            if (lane == 0 && vuse > 0) wait_or_abort(&bs->v_empty[vs], (vuse - 1) & 1, bs, p.status);
+            __syncwarp();
+            if (aborted(bs)) break;
+            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->v_full[vs], kSlotBytes);
+            __syncwarp();
+            uint8_t *sV = sm + kOffV + vs * kSlotBytes;
+            if (lane < kPagesPerBlock) {
+                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->v_full[vs], 0, g, 0, page);
+                tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->v_full[vs], 64, g, 0, page);
+            }
+            ++nv;
         }
         if (aborted(bs) && lane == 0) {
             // drain copies that may still be landing in this CTA's shared memory
             tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
-            for (int it = max(0, nb - kStages); it < nb; ++it)
-                tc::mbar_wait(&bs->kv_full[it % kStages], (it / kStages) & 1, kWaitBudget);
+            for (int i = max(0, nk - kKStages); i < nk; ++i)
+                tc::mbar_wait(&bs->k_full[i % kKStages], (i / kKStages) & 1, kWaitBudget);
+            for (int i = max(0, nv - kVStages); i < nv; ++i)
+                tc::mbar_wait(&bs->v_full[i % kVStages], (i / kVStages) & 1, kWaitBudget);
         }
     } else if (warp == kMmaWarp) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            auto issue_s = [&](int it, int t) {  // S(it) of tile t into S buffer it & 1
-                const int sb = it & 1, st = it % kStages;
-                const uint32_t k_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes);
+            auto issue_s = [&](int it, int t) {  // S(it) of tile t: 8 MMAs M128 N128 K16
+                const uint32_t k_addr = tc::smem_u32(sm + kOffK + (it % kKStages) * kSlotBytes);
                 const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
 #pragma unroll
                 for (int kk = 0; kk < 8; ++kk) {
                     const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
                     const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                    tc::mma_bf16_ss(tmem + t * 128 + sb * kBlockKV, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
+                    tc::mma_bf16_ss(tmem + t * 128, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
                                     tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
                 }
-                tc::mma_commit(&bs->s_full[t][sb]);
+                tc::mma_commit(&bs->s_full[t]);
+                if (t == kTiles - 1) tc::mma_commit(&bs->k_empty[it % kKStages]);
             };
             bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
-            for (int it = 0; it < min(nb, 2) && ok; ++it) {
-                ok = wait_or_abort(&bs->kv_full[it % kStages], (it / kStages) & 1, bs, p.status);
-                if (!ok) break;
+            ok = ok && wait_or_abort(&bs->k_full[0], 0, bs, p.status);
+            if (ok) {
                 tc::tc_fence_after();
-                for (int t = 0; t < kTiles; ++t) issue_s(it, t);
+                for (int t = 0; t < kTiles; ++t) issue_s(0, t);
             }
+            // Per block and tile: PV(it) once the tile's P is in TMEM, then
+            // S(it + 1) once PV(it) has read P (S and P share the columns).
+            // The other tile's softmax runs meanwhile, so the tensor pipe
+            // alternates between the tiles.
             for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
-                const int pb = it & 1, st = it % kStages;
-                const uint32_t v_addr = tc::smem_u32(sm + kOffKV + st * kStageBytes + 2 * kKVHalf);
+                const int vs = it % kVStages;
+                const uint32_t v_addr = tc::smem_u32(sm + kOffV + vs * kSlotBytes);
                 for (int t = 0; t < kTiles && ok; ++t) {
-                    if (!wait_or_abort(&bs->p_full[t][pb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+                    if (!wait_or_abort(&bs->p_full[t], it & 1, bs, p.status)) { ok = false; break; }
+                    if (t == 0 && !wait_or_abort(&bs->v_full[vs], (it / kVStages) & 1, bs, p.status)) { ok = false; break; }
                     tc::tc_fence_after();
-                    const uint32_t p_tmem = tmem + t * 128 + pb * kBlockKV;
 #pragma unroll
                     for (int kk = 0; kk < kBlockKV / 16; ++kk) {
-                        tc::mma_bf16_ts(tmem + kColO + t * 128, p_tmem + kk * 8,
+                        tc::mma_bf16_ts(tmem + kColO + t * 128, tmem + t * 128 + kk * 8,
                                         tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
                                         (it > 0 || kk > 0) ? 1u : 0u);
                     }
-                    tc::mma_commit(&bs->p_free[t][pb]);
-                }
-                if (!ok) break;
-                tc::mma_commit(&bs->kv_empty[st]);
-                const int in = it + 2;  // S(it + 2) reuses the buffer that holds P(it)
-                if (in < nb) {
-                    if (!wait_or_abort(&bs->kv_full[in % kStages], (in / kStages) & 1, bs, p.status)) { ok = false; break; }
-                    for (int t = 0; t < kTiles && ok; ++t) {
-                        // PV(it) of tile t has read P(it) from the buffer (this overlaps PV(it) of the next tile)
-                        if (!wait_or_abort(&bs->p_free[t][pb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+                    tc::mma_commit(&bs->p_free[t]);
+                    if (t == kTiles - 1) tc::mma_commit(&bs->v_empty[vs]);
+                    if (it + 1 < nb) {
+                        if (t == 0 && !wait_or_abort(&bs->k_full[(it + 1) % kKStages], ((it + 1) / kKStages) & 1, bs,
+                                                     p.status)) { ok = false; break; }
+                        if (!wait_or_abort(&bs->p_free[t], it & 1, bs, p.status)) { ok = false; break; }
                         tc::tc_fence_after();
-                        issue_s(in, t);
+                        issue_s(it + 1, t);
                     }
                 }
             }
@@ -342,26 +365,27 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         float m_ref = -INFINITY, lsum = 0.0f;
         bool ok = true;
         for (int it = 0; it < nb && ok; ++it) {
-            const int sb = it & 1;
             const int p0 = (blk0 + it) * kBlockKV;
-            if (!wait_or_abort(&bs->s_full[tile][sb], (it >> 1) & 1, bs, p.status)) { ok = false; break; }
+            if (!wait_or_abort(&bs->s_full[tile], it & 1, bs, p.status)) { ok = false; break; }
             tc::tc_fence_after();
-            float x[kBlockKV];
-            tc::tmem_ld64(tmem + lane_base + col_s + sb * kBlockKV, x);
+            float xa[64], xb[64];  // keys 0-63 and 64-127 of the block
+            tc::tmem_ld64(tmem + lane_base + col_s, xa);
+            tc::tmem_ld64(tmem + lane_base + col_s + 64, xb);
+#define X(c) ((c) < 64 ? xa[(c) & 63] : xb[(c) & 63])
             // mask (raw scores) and block max
             if (live && p0 + kBlockKV > L) {
 #pragma unroll
                 for (int c = 0; c < kBlockKV; ++c) {
                     const int jt = p0 + c - L;
                     const bool vis = jt < 0 || (jt <= node && ((anc >> (jt & 63)) & 1ull));
-                    x[c] = vis ? x[c] : -INFINITY;
+                    if (!vis) X(c) = -INFINITY;
                 }
             }
             float mx8[8];  // 8 independent chains, then a tree
 #pragma unroll
-            for (int q = 0; q < 8; ++q) mx8[q] = x[q];
+            for (int q = 0; q < 8; ++q) mx8[q] = xa[q];
 #pragma unroll
-            for (int c = 8; c < kBlockKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], x[c]);
+            for (int c = 8; c < kBlockKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], X(c));
             const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
                                    fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
             const float mb = mx * sl2;  // scale > 0: max commutes with scaling
@@ -377,10 +401,29 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     rescale = true;
                 }
             }
+            const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
+            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+            // P as bf16 pairs (lower key in the low half) over the first 64
+            // columns of the S buffer, in four stores of 32 keys (S is in
+            // registers, so overwriting its columns is safe), one wait at the end.
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                uint32_t pw[16];
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const float a0 = tc::ex2(fmaf(X(32 * h + 2 * c), sl2, neg));
+                    const float a1 = tc::ex2(fmaf(X(32 * h + 2 * c + 1), sl2, neg));
+                    pw[c] = pack_bf16x2(a0, a1);
+                    ls[(2 * c) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
+                    ls[(2 * c + 1) & 7] += a1;
+                }
+                tc::tmem_st16u_nowait(tmem + lane_base + col_s + 16 * h, pw);
+            }
+            tc::tmem_wait_st();
+            lsum = lsum * alpha + (((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7])));
+            // Rescale O (after the scores are dead, before PV(it) may start):
+            // PV(it-1) has completed, since S(it) was computed after it.
             if (__any_sync(0xffffffffu, rescale) && it > 0) {
-                // PV(it-1) must have landed in O before it is rescaled
-                if (!wait_or_abort(&bs->p_free[tile][(it - 1) & 1], ((it - 1) >> 1) & 1, bs, p.status)) { ok = false; break; }
-                tc::tc_fence_after();
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
@@ -390,26 +433,12 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc::tmem_st32(tmem + lane_base + col_o + c * 32, o);
                 }
             }
-            lsum *= alpha;
-            const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
-            uint32_t pw[kBlockKV / 2];  // P row as bf16 pairs, lower key in the low half
-            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
-#pragma unroll
-            for (int c = 0; c < kBlockKV / 2; ++c) {
-                const float a0 = tc::ex2(fmaf(x[2 * c], sl2, neg));
-                const float a1 = tc::ex2(fmaf(x[2 * c + 1], sl2, neg));
-                pw[c] = pack_bf16x2(a0, a1);
-                ls[(2 * c) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
-                ls[(2 * c + 1) & 7] += a1;
-            }
-            lsum += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
-            // P over the first 32 columns of this S buffer (S is already in registers)
-            tc::tmem_st32u(tmem + lane_base + col_s + sb * kBlockKV, pw);
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->p_full[tile][sb]);
+            tc::mbar_arrive(&bs->p_full[tile]);
+#undef X
         }
         // ---------------- epilogue ----------------
-        if (ok && wait_or_abort(&bs->p_free[tile][(nb - 1) & 1], ((nb - 1) >> 1) & 1, bs, p.status)) {
+        if (ok && wait_or_abort(&bs->p_free[tile], (nb - 1) & 1, bs, p.status)) {
             tc::tc_fence_after();
             const size_t row = ((size_t)b * p.N + node) * p.Hq + row_head;
             const bool write = node < p.N;
