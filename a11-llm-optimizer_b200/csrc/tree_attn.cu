@@ -131,6 +131,13 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a0, float a1) {
     return __byte_perm(__float_as_uint(a0) + 0x8000u, __float_as_uint(a1) + 0x8000u, 0x7632);
 }
 
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
 __global__ void __launch_bounds__(kTcThreads, 1)
     tree_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const TcParams p) {
@@ -381,13 +388,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     if (!vis) X(c) = -INFINITY;
                 }
             }
-            float mx8[8];  // 8 independent chains, then a tree
+            float mx8[8];  // 8 independent chains of three-input maxima, then a tree
 #pragma unroll
             for (int q = 0; q < 8; ++q) mx8[q] = xa[q];
 #pragma unroll
-            for (int c = 8; c < kBlockKV; ++c) mx8[c & 7] = fmaxf(mx8[c & 7], X(c));
-            const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                   fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+            for (int c = 8; c + 16 <= kBlockKV; c += 16)
+#pragma unroll
+                for (int q = 0; q < 8; ++q) mx8[q] = fmax3(mx8[q], X(c + q), X(c + 8 + q));
+#pragma unroll
+            for (int q = 0; q < 8; ++q) mx8[q] = fmaxf(mx8[q], X(kBlockKV - 8 + q));
+            const float mx = fmax3(fmax3(mx8[0], mx8[1], mx8[2]), fmax3(mx8[3], mx8[4], mx8[5]),
+                                   fmaxf(mx8[6], mx8[7]));
             const float mb = mx * sl2;  // scale > 0: max commutes with scaling
             // lazy rescale of (O, l)
             float alpha = 1.0f;
