@@ -91,10 +91,13 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()  # the timed region starts once samples flow
+            while not self.lines and time.time() - t0 < 3.0:
+                time.sleep(0.01)
         except (OSError, FileNotFoundError):
             self.proc = None
         return self
@@ -240,11 +243,14 @@ def run_ours(args, rank, world, local_rank):
     barrier()
     s1 = stats.clone()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    x0.record()
-    for _ in range(args.steps):
-        e2e_step()
-    x1.record()
-    barrier()
+    with ClockSampler(gpu_id(dev)) as clk_e2e:  # the clock record covers both timed regions
+        barrier()
+        x0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        x1.record()
+        barrier()
+    clk.lines.extend(clk_e2e.lines)
     e2e_ms = x0.elapsed_time(x1)
     e2e_emitted = int((stats - s1)[a11spec.STAT_NAMES.index("emitted_tokens")])
 
