@@ -1,17 +1,22 @@
 // accept.cu - K3: vocab-wide softmax/argmax + acceptance + path select + bonus draw.
 //
-// One kernel per call.
+// One kernel per call; block (x, y) = (sequence, slice of its units), so the
+// first wave holds every sequence's first slice.
 // Phase 1 (every block, HBM-bound): warps stream 2048-token chunks of every
-//   live logits row with 16-byte non-allocating loads and keep one number per
-//   chunk: its maximum (NaN-propagating, so a NaN or +Inf is caught here).
-//   That is two instructions per logit, the single read of the vocab.
-// Phase 2 (the block that completes a sequence, found with a fenced atomic
-//   counter; nothing waits): walk the tree from the root.
+//   live logits row with 16-byte non-allocating loads and keep the chunk
+//   maximum (NaN-propagating, so a NaN or +Inf is caught here): two
+//   instructions per logit, the single read of the vocab. A sequence's units
+//   start with its root rows; only their maxima are recorded (and, in the
+//   sampling modes, their fixed-point weight sums).
+// Phase 2 (the block that completes a sequence's root rows, found with a
+//   fenced atomic counter; nothing waits): walk the tree from the root while
+//   the bulk pass goes on in other blocks.
 //   GREEDY  row argmax = first chunk holding the row max, then the first token
-//           equal to it inside that chunk (one 2048-token rescan per visited row).
+//           equal to it inside that chunk.
 //   STOCH_* the fixed-point softmax statistics (frame c_j = ceil(cmax_j * k),
-//           S_j = sum of weights) are computed for the rows the walk visits only,
-//           by all 16 warps; then acceptance, residuals and the bonus draw.
+//           S_j = sum of weights); then acceptance, residuals and the bonus draw.
+//   Rows other than the root are read again by the walking block for their
+//   chunk maxima and weights, for the rows the walk visits only.
 // The numbers are exactly those of the oracle (order-independent integer
 // sums), so decisions are bit-exact.
 //
@@ -136,6 +141,7 @@ struct WalkSmem {
     int32_t kids[A11S_MAX_ACCEPT_NODES];  // children of the current node, index order
     float kl[A11S_MAX_ACCEPT_NODES];      // their target logits
     float kq[A11S_MAX_ACCEPT_NODES];      // and draft logits (DRAFT)
+    float cmx[kMaxNch];     // chunk maxima of the row being visited (GREEDY argmax)
     float cp[A11S_CHUNK];   // one staged chunk of the p row (widened to fp32)
     float cq[A11S_CHUNK];   // and of the q row (DRAFT)
     uint64_t wtot[kWarps];  // per-warp weight totals of the bonus scan
@@ -206,38 +212,64 @@ __device__ RowStat combine_sums(const int32_t *fr, const uint64_t *sum, int nch,
     return rs;
 }
 
-// Every warp of the block: frames and weight sums of one row into fr/sum.
+// Every warp of the block: frames and weight sums of one non-root row into
+// fr/sum. The row's chunk maxima are taken here (the bulk pass keeps only the
+// root rows' records), then each chunk's weights in its frame (a second read
+// of the chunk, from L2). A non-finite logit or an out-of-range frame is
+// reported like in the bulk pass.
 template <bool BF16>
-__device__ void row_sums(const char *row, const float *cmax, int nch, int V, float k, int32_t *fr, uint64_t *sum,
-                         int warp, int lane) {
+__device__ void row_sums(const char *row, int nch, int V, float k, int32_t *fr, uint64_t *sum, int warp, int lane,
+                         StatusWord *st, int b) {
+    int bad = 0;
     for (int j = warp; j < nch; j += kWarps) {
-        const float cm = __ldcg(cmax + j);
-        const int32_t f = frame_of(cm, k);
+        const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+        const float cm = chunk_max<BF16>(row, c0, clen, lane);
+        bad |= !(cm < INFINITY) || (cm > -INFINITY && !(fabsf(__fmul_rn(cm, k)) < 16777216.0f));
+        const int32_t f = cm < INFINITY ? frame_of(cm, k) : A11S_FRAME_NONE;
         uint64_t s = 0;
-        if (f != A11S_FRAME_NONE) {
-            const int c0 = j * A11S_CHUNK;
-            s = chunk_wsum<BF16>(row, c0, min(A11S_CHUNK, V - c0), k, (float)f, lane);
-        }
+        if (f != A11S_FRAME_NONE) s = chunk_wsum<BF16>(row, c0, clen, k, (float)f, lane);
         if (lane == 0) {
             fr[j] = f;
             sum[j] = s;
         }
     }
+    if (bad && lane == 0) report(st, A11S_ENONFINITE, b);
 }
 
-// Frames and weight sums of a row: the root's come from phase 1, the others
-// are computed by every warp of the block.
+// Frames and weight sums of a row: the root's come from the bulk pass (chunk
+// records and weight sums), the others are computed by every warp of the block.
 template <bool BF16>
-__device__ void row_stats_into(const char *row, const float *cmax, const unsigned long long *root, int nch, int V,
-                               float k, int32_t *fr, uint64_t *sum, int warp, int lane) {
+__device__ void row_stats_into(const char *row, const float *root_cmax, const unsigned long long *root, int nch,
+                               int V, float k, int32_t *fr, uint64_t *sum, int warp, int lane, StatusWord *st,
+                               int b) {
     if (root) {
         for (int j = threadIdx.x; j < nch; j += blockDim.x) {
-            fr[j] = frame_of(__ldcg(cmax + j), k);
+            fr[j] = frame_of(__ldcg(root_cmax + j), k);
             sum[j] = __ldcg(root + j);
         }
     } else {
-        row_sums<BF16>(row, cmax, nch, V, k, fr, sum, warp, lane);
+        row_sums<BF16>(row, nch, V, k, fr, sum, warp, lane, st, b);
     }
+}
+
+// Chunk maxima of a row into shared memory (every thread of the block): the
+// root's are copied from the bulk pass's records, the others are computed.
+template <bool BF16>
+__device__ void row_cmax_into(const char *row, const float *root_cmax, int nch, int V, float *dst, int warp,
+                              int lane, StatusWord *st, int b) {
+    if (root_cmax) {
+        for (int j = threadIdx.x; j < nch; j += blockDim.x) dst[j] = __ldcg(root_cmax + j);
+    } else {
+        int bad = 0;
+        for (int j = warp; j < nch; j += kWarps) {
+            const int c0 = j * A11S_CHUNK;
+            const float cm = chunk_max<BF16>(row, c0, min(A11S_CHUNK, V - c0), lane);
+            bad |= !(cm < INFINITY);
+            if (lane == 0) dst[j] = cm;
+        }
+        if (bad && lane == 0) report(st, A11S_ENONFINITE, b);
+    }
+    __syncthreads();
 }
 
 __device__ __forceinline__ double chunk_scale(const RowStat &rs, int32_t frame) {
@@ -357,13 +389,13 @@ __device__ bool pick_chunk(float u, const uint64_t *A, const uint64_t *Lc, int n
 // first token equal to it in that chunk (staged in shared memory).
 template <bool BF16>
 __device__ int row_argmax(const char *row, const float *cmax, int nch, int V, float *stage, int lane) {
-    float M = -INFINITY;
-    for (int j = lane; j < nch; j += 32) M = fmaxf(M, __ldcg(cmax + j));
+    float M = -INFINITY;  // cmax: the row's chunk maxima in shared memory
+    for (int j = lane; j < nch; j += 32) M = fmaxf(M, cmax[j]);
     M = warp_fmax(M);
     int jstar = INT_MAX;
     for (int j0 = 0; j0 < nch && jstar == INT_MAX; j0 += 32) {
         const int j = j0 + lane;
-        const unsigned hit = __ballot_sync(0xffffffffu, j < nch && __ldcg(cmax + j) == M);
+        const unsigned hit = __ballot_sync(0xffffffffu, j < nch && cmax[j] == M);
         if (hit) jstar = j0 + __ffs(hit) - 1;
     }
     if (jstar == INT_MAX) return 0;  // unreachable for rows without NaN
@@ -384,17 +416,33 @@ __device__ int row_argmax(const char *row, const float *cmax, int nch, int V, fl
 // ---------------------------------------------------------------------------
 template <int MODE, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a) {
-    const int b = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
     const bool seq_ok = n_live >= 1 && n_live <= a.N;
     if (!seq_ok) n_live = 0;
     const size_t row_bytes = (size_t)a.stride * (BF16 ? 2 : 4);
 
     // ---------------- phase 1: chunk maxima ----------------
-    const int u0 = blockIdx.x * a.slice, u1 = min(u0 + a.slice, a.units_per_seq);
+    // Units of a sequence: first the root rows' chunks (the p root, and the q
+    // root in DRAFT mode), then the other rows' chunks, rows fastest. The
+    // block that completes the root rows walks the tree while the bulk pass
+    // goes on in other blocks: the walk needs the root rows' records and
+    // computes the statistics of the other rows it visits itself.
+    constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
+    const int n_root_units = kRootRows * a.nch;
+    const int u0 = blockIdx.y * a.slice, u1 = min(u0 + a.slice, a.units_per_seq);
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += kWarps) {
-        const int j = u / a.rows_per_seq, r = u - j * a.rows_per_seq;  // rows fastest
+        int j, r;
+        if (u < n_root_units) {
+            j = u / kRootRows;
+            r = (u - j * kRootRows) ? a.N : 0;
+        } else {
+            const int v = u - n_root_units, other = a.rows_per_seq - kRootRows;
+            j = v / other;
+            const int q = v - j * other;  // 1..N-1 (p rows), then N+1..2N-1 (q rows)
+            r = q < a.N - 1 ? 1 + q : a.N + 1 + (q - (a.N - 1));
+        }
         const bool isq = r >= a.N;
         const int node = isq ? r - a.N : r;
         if (node >= n_live) continue;
@@ -403,7 +451,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         const float m = chunk_max<BF16>(row, c0, clen, lane);
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
-        if (lane == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = m;
+        if (lane == 0 && node == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = m;
         if (MODE != A11S_ACCEPT_GREEDY && node == 0) {
             // The walk always starts at the root: its weight sums are taken
             // here, while the chunk is hot in L2, instead of in the walk.
@@ -417,9 +465,12 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     __syncthreads();
     __shared__ int s_last;
     if (threadIdx.x == 0) {
-        const int done = u1 - u0;
-        const int prev = atomicAdd(&a.counters[b], done);
-        s_last = (prev + done == a.units_per_seq);
+        const int done = max(0, min(u1, n_root_units) - u0);  // root units of this block
+        s_last = 0;
+        if (done > 0) {
+            const int prev = atomicAdd(&a.counters[b], done);
+            s_last = (prev + done == n_root_units);
+        }
     }
     __syncthreads();
     if (!s_last) return;
@@ -469,8 +520,8 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             for (int c = r + 1; c < n_live && !has_child; ++c) has_child = sm.par[c] == r;
             if (!has_child) continue;
             const char *prow = tgt_b + (size_t)r * row_bytes;
-            row_stats_into<BF16>(prow, cmax_b + (size_t)r * nch, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr,
-                                 nch, V, a.k, sm.fr, sm.sum, warp, lane);
+            row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, nch, V, a.k,
+                                 sm.fr, sm.sum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
                 const RowStat rs = combine_sums(sm.fr, sm.sum, nch, lane);
@@ -488,21 +539,31 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     int alen = 0, node = 0, bonus = -1;
     bool failed = false;
     if (MODE == A11S_ACCEPT_GREEDY) {
-        if (warp == 0) {
-            for (;;) {
-                const int am = row_argmax<BF16>(tgt_b + (size_t)node * row_bytes, cmax_b + (size_t)node * nch, nch,
-                                                V, sm.cp, lane);
+        // Every warp takes the chunk maxima of a visited non-root row; warp 0
+        // finds the argmax and the matching child.
+        for (;;) {
+            const char *row = tgt_b + (size_t)node * row_bytes;
+            row_cmax_into<BF16>(row, node == 0 ? cmax_b : nullptr, nch, V, sm.cmx, warp, lane, a.status, b);
+            if (warp == 0) {
+                const int am = row_argmax<BF16>(row, sm.cmx, nch, V, sm.cp, lane);
                 int next = INT_MAX;
                 for (int c0 = node + 1; c0 < n_live && next == INT_MAX; c0 += 32) {
                     const int c = c0 + lane;
                     const unsigned m = __ballot_sync(0xffffffffu, c < n_live && sm.par[c] == node && sm.tok[c] == am);
                     if (m) next = c0 + __ffs(m) - 1;
                 }
-                if (next == INT_MAX) { bonus = am; break; }
-                if (lane == 0) { an[alen] = next; at[alen] = sm.tok[next]; }
-                ++alen;
-                node = next;
+                if (next == INT_MAX) {
+                    bonus = am;
+                } else {
+                    if (lane == 0) { an[alen] = next; at[alen] = sm.tok[next]; }
+                    ++alen;
+                }
+                if (lane == 0) sm.child = next == INT_MAX ? -1 : next;
             }
+            __syncthreads();
+            node = sm.child;
+            __syncthreads();  // every thread has read sm.child before warp 0 rewrites it
+            if (node < 0) break;
         }
     } else {
         // Sampling walk. Every warp computes a visited row's statistics (and the
@@ -514,10 +575,10 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             const unsigned long long *rs_p = nd == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr;
             const char *prow = tgt_b + (size_t)nd * row_bytes;
             const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
-            row_stats_into<BF16>(prow, cmax_b + (size_t)nd * nch, rs_p, nch, V, a.k, sm.fr, sm.sum, warp, lane);
+            row_stats_into<BF16>(prow, cmax_b, rs_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
             if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                row_stats_into<BF16>(qrow, cmax_b + (size_t)(N + nd) * nch, nd == 0 ? rs_p + nch : nullptr, nch, V,
-                                     a.k, sm.qfr, sm.qsum, warp, lane);
+                row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, nch, V, a.k,
+                                     sm.qfr, sm.qsum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
                 sm.ps = combine_sums(sm.fr, sm.sum, nch, lane);
@@ -782,7 +843,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
 }
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_x, cudaStream_t s) {
-    dim3 grid(grid_x, a.B), block(kThreads);
+    dim3 grid(a.B, grid_x), block(kThreads);  // sequences fastest: every root block in the first wave
 #define A11S_LAUNCH(M, BF)                                                   \
     if (mode == M && bf16 == BF) {                                           \
         accept_kernel<M, BF><<<grid, block, 0, s>>>(a);                      \

@@ -23,7 +23,7 @@ struct AcceptArgs {
     int32_t *bonus;
     float *node_probs;
     long long *stats;
-    float *recs;  // [B][rows_per_seq][nch] chunk maxima (NaN-propagating)
+    float *recs;  // [B][rows_per_seq][nch] chunk maxima (NaN-propagating); written for the root rows only
     unsigned long long *root_sums;  // [B][2][nch] weight sums of the root rows (p, q)
     int32_t *counters;
     StatusWord *status;
