@@ -8,9 +8,9 @@
 //   instructions per logit, the single read of the vocab. A sequence's units
 //   start with its root rows; only their maxima are recorded (and, in the
 //   sampling modes, their fixed-point weight sums).
-// Phase 2 (the block that completes a sequence's root rows, found with a
-//   fenced atomic counter; nothing waits): walk the tree from the root while
-//   the bulk pass goes on in other blocks.
+// Phase 2 (the block of slice 0, which holds exactly the sequence's root-row
+//   units; nothing waits): walk the tree from the root while the bulk pass
+//   goes on in other blocks.
 //   GREEDY  row argmax = first chunk holding the row max, then the first token
 //           equal to it inside that chunk.
 //   STOCH_* the fixed-point softmax statistics (frame c_j = ceil(cmax_j * k),
@@ -424,13 +424,14 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
 
     // ---------------- phase 1: chunk maxima ----------------
     // Units of a sequence: first the root rows' chunks (the p root, and the q
-    // root in DRAFT mode), then the other rows' chunks, rows fastest. The
-    // block that completes the root rows walks the tree while the bulk pass
-    // goes on in other blocks: the walk needs the root rows' records and
+    // root in DRAFT mode), then the other rows' chunks, rows fastest. Slice 0
+    // is exactly the root units; its block then walks the tree while the bulk
+    // pass goes on in other blocks: the walk needs the root rows' records and
     // computes the statistics of the other rows it visits itself.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
-    const int u0 = blockIdx.y * a.slice, u1 = min(u0 + a.slice, a.units_per_seq);
+    const int u0 = blockIdx.y == 0 ? 0 : n_root_units + (blockIdx.y - 1) * a.slice;
+    const int u1 = blockIdx.y == 0 ? n_root_units : min(u0 + a.slice, a.units_per_seq);
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += kWarps) {
         int j, r;
@@ -451,7 +452,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         const float m = chunk_max<BF16>(row, c0, clen, lane);
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
-        if (lane == 0 && node == 0) a.recs[((size_t)b * a.rows_per_seq + r) * a.nch + j] = m;
+        if (lane == 0 && node == 0) a.recs[((size_t)b * kRootRows + (isq ? 1 : 0)) * a.nch + j] = m;
         if (MODE != A11S_ACCEPT_GREEDY && node == 0) {
             // The walk always starts at the root: its weight sums are taken
             // here, while the chunk is hot in L2, instead of in the walk.
@@ -461,27 +462,15 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         }
     }
     if (warp_or(bad) && lane == 0) report(a.status, A11S_ENONFINITE, b);
-    __threadfence();
-    __syncthreads();
-    __shared__ int s_last;
-    if (threadIdx.x == 0) {
-        const int done = max(0, min(u1, n_root_units) - u0);  // root units of this block
-        s_last = 0;
-        if (done > 0) {
-            const int prev = atomicAdd(&a.counters[b], done);
-            s_last = (prev + done == n_root_units);
-        }
-    }
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
+    if (blockIdx.y != 0) return;
+    __syncthreads();  // the root rows' records and weight sums were written by this block
 
     // ---------------- phase 2: walk ----------------
     __shared__ WalkSmem sm;
     const int N = a.N, V = a.V, nch = a.nch;
     int32_t *an = a.acc_nodes + (size_t)b * N;
     int32_t *at = a.acc_tokens + (size_t)b * N;
-    const float *cmax_b = a.recs + (size_t)b * a.rows_per_seq * nch;
+    const float *cmax_b = a.recs + (size_t)b * kRootRows * nch;  // root rows' chunk maxima (p, then q)
     const char *tgt_b = reinterpret_cast<const char *>(a.target) + (size_t)b * N * row_bytes;
     const char *drf_b = MODE == A11S_ACCEPT_STOCH_DRAFT
                             ? reinterpret_cast<const char *>(a.draft) + (size_t)b * N * row_bytes
@@ -577,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
             row_stats_into<BF16>(prow, cmax_b, rs_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
             if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, nch, V, a.k,
+                row_stats_into<BF16>(qrow, cmax_b + nch, nd == 0 ? rs_p + nch : nullptr, nch, V, a.k,
                                      sm.qfr, sm.qsum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
@@ -842,8 +831,8 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         for (int i = lane; i < N; i += 32) { an[i] = -1; at[i] = -1; }
 }
 
-cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_x, cudaStream_t s) {
-    dim3 grid(a.B, grid_x), block(kThreads);  // sequences fastest: every root block in the first wave
+cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s) {
+    dim3 grid(a.B, grid_y), block(kThreads);  // sequences fastest: every root block in the first wave
 #define A11S_LAUNCH(M, BF)                                                   \
     if (mode == M && bf16 == BF) {                                           \
         accept_kernel<M, BF><<<grid, block, 0, s>>>(a);                      \

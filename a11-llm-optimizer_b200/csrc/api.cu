@@ -48,16 +48,18 @@ int sm_count() {
 }
 
 // ---- acceptance workspace layout ----
+// status word | chunk maxima of the root rows [B][root rows][nch] float |
+// weight sums of the root rows [B][2][nch] uint64 (sampling modes)
 struct AcceptLayout {
-    size_t counters, recs, root_sums, total;
+    size_t recs, root_sums, total;
 };
 AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
+    (void)max_nodes;
     AcceptLayout L;
     const size_t nch = (size_t)(vocab + A11S_CHUNK - 1) / A11S_CHUNK;
-    const size_t rows = (size_t)batch * max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
-    L.counters = kHeaderBytes;
-    L.recs = L.counters + up256(sizeof(int32_t) * (size_t)batch);
-    L.root_sums = L.recs + up256(rows * nch * sizeof(float));
+    const size_t root_rows = (size_t)batch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    L.recs = kHeaderBytes;
+    L.root_sums = L.recs + up256(root_rows * nch * sizeof(float));
     L.total = L.root_sums + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * 2 * nch * sizeof(uint64_t)));
     return L;
 }
@@ -156,25 +158,27 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.stats = reinterpret_cast<long long *>(stats);
     char *ws = static_cast<char *>(workspace);
     a.status = reinterpret_cast<a11s::StatusWord *>(ws);
-    a.counters = reinterpret_cast<int32_t *>(ws + L.counters);
     a.recs = reinterpret_cast<float *>(ws + L.recs);
     a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
 
-    // Balance: about 4 waves of 2 resident 512-thread blocks per SM, at least
+    // Slice 0 of a sequence is exactly its root rows' units, so that block
+    // reads only the root rows before it walks the tree. The other units are
+    // balanced: about 4 waves of 2 resident 512-thread blocks per SM, at least
     // 16 chunks (one per warp) per block.
-    const long long total_units = (long long)batch * a.units_per_seq;
+    const int root_units = a.nch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    const long long rest = (long long)a.units_per_seq - root_units;
     const long long target_blocks = (long long)sm_count() * 2 * 4;
-    long long slice = (total_units + target_blocks - 1) / target_blocks;
+    long long slice = ((long long)batch * rest + target_blocks - 1) / target_blocks;
     slice = ((slice + 15) / 16) * 16;
     if (slice < 16) slice = 16;
-    if (slice > a.units_per_seq) slice = a.units_per_seq;
+    if (slice > rest && rest > 0) slice = rest;
     a.slice = (int32_t)slice;
-    const int grid_x = (a.units_per_seq + a.slice - 1) / a.slice;
+    const int grid_y = 1 + (int)((rest + slice - 1) / slice);
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(ws, 0, L.recs, s);  // status word + per-sequence counters
+    cudaError_t e = cudaMemsetAsync(ws, 0, kHeaderBytes, s);  // the status word
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: clearing workspace");
-    e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_x, s);
+    e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_y, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: launch");
     return A11S_OK;
 }

@@ -23,13 +23,12 @@ struct AcceptArgs {
     int32_t *bonus;
     float *node_probs;
     long long *stats;
-    float *recs;  // [B][rows_per_seq][nch] chunk maxima (NaN-propagating); written for the root rows only
+    float *recs;  // [B][root rows: 1, or 2 in DRAFT][nch] chunk maxima of the root rows (NaN-propagating)
     unsigned long long *root_sums;  // [B][2][nch] weight sums of the root rows (p, q)
-    int32_t *counters;
     StatusWord *status;
 };
 
-cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_x, cudaStream_t s);
+cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s);
 
 struct CompactArgs {
     char *k_pool;

@@ -84,7 +84,7 @@ def test_static_scratch_matches_workspace_entry_point(dev, mode, dtype):
 
 def test_static_scratch_rejects_oversize_without_launching(dev):
     f = _bind()
-    B, N, V = 256, 64, 151936  # 256 * 64 * 75 chunk records of 4 B > 4 MiB
+    B, N, V = 65536, 64, 151936  # 65536 sequences x 75 root-row chunk records of 4 B > 4 MiB
     need = a11spec.ops.accept_workspace_bytes(_lib.GREEDY, B, N, V)
     assert need > (4 << 20)
     logits = torch.zeros(1, dtype=torch.float32, device="cuda")  # never read
