@@ -4,6 +4,7 @@
     python a11-llm-optimizer_b200/a11spec/cases.py accept --mode onehot --batch 32 --iters 2
     python a11-llm-optimizer_b200/a11spec/cases.py compact --batch 32 --ctx 4096 --iters 2
     python a11-llm-optimizer_b200/a11spec/cases.py ngram --batch 32 --iters 2
+    python a11-llm-optimizer_b200/a11spec/cases.py pages --batch 32 --ctx 32768 --iters 20
 
 Each case builds its inputs on cuda:0 (seeded), runs the kernel `--warmup`
 times, then `--iters` times between CUDA events, and prints one JSON line
@@ -126,9 +127,53 @@ def case_ngram(a) -> dict:
     return {"case": "ngram", "batch": a.batch, "us": us}
 
 
+def case_pages(a) -> dict:
+    """Page allocator per decode step: reserve the tree slots of every sequence
+    (a11s_kv_reserve), then hand the tree's pages back (a11s_kv_release), as
+    after a compaction that kept nothing. Each launch is timed with its own
+    CUDA events; the torch ops that rebuild the freed lists sit between them."""
+    dev = "cuda"
+    B, MP = a.batch, (a.ctx + a.nodes + 15) // 16 + 1
+    pool = a11spec.ops.KVPagePool(B * MP, dev)
+    pt = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+    sl = torch.zeros(B, dtype=torch.int32, device=dev)
+    pool.reserve(pt, sl, torch.full((B,), a.ctx, dtype=torch.int32, device=dev), check_status=True)
+    n_new = torch.full((B,), a.nodes, dtype=torch.int32, device=dev)
+    freed = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+    nfreed = torch.zeros(B, dtype=torch.int32, device=dev)
+    p0 = (a.ctx + 15) // 16
+    span = (a.ctx + a.nodes + 15) // 16 - p0
+    ev = []
+
+    def run(timed):
+        e = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+        e[0].record()
+        pool.reserve(pt, sl, n_new)  # tree slots
+        e[1].record()
+        sl.sub_(n_new)
+        freed[:, :span] = pt[:, p0:p0 + span]
+        pt[:, p0:p0 + span] = -1
+        nfreed.fill_(span)
+        e[2].record()
+        pool.release(freed, nfreed)
+        e[3].record()
+        if timed:
+            ev.append(e)
+
+    for _ in range(a.warmup):
+        run(False)
+    for _ in range(a.iters):
+        run(True)
+    torch.cuda.synchronize()
+    res = sum(x[0].elapsed_time(x[1]) for x in ev) * 1e3 / len(ev)
+    rel = sum(x[2].elapsed_time(x[3]) for x in ev) * 1e3 / len(ev)
+    return {"case": "pages", "batch": B, "ctx": a.ctx, "nodes": a.nodes, "reserve_us": res, "release_us": rel,
+            "pages_per_step": B * span, "status": [int(x) for x in pool.status.tolist()]}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram"])
+    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram", "pages"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--nodes", type=int, default=64)
@@ -137,7 +182,8 @@ def main(argv=None) -> None:
     ap.add_argument("--iters", type=int, default=2)
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
-    fn = {"attention": case_attention, "accept": case_accept, "compact": case_compact, "ngram": case_ngram}[a.case]
+    fn = {"attention": case_attention, "accept": case_accept, "compact": case_compact, "ngram": case_ngram,
+          "pages": case_pages}[a.case]
     print(json.dumps(fn(a)), flush=True)
 
 

@@ -105,6 +105,10 @@ class PagedKVCacheManager:
             raise RuntimeError("PagedKVCache: sequence not active")
         return list(s.block_table)
 
+    def free_stack(self) -> List[int]:
+        """The free page ids, bottom of the stack first (the next pop is the last)."""
+        return list(self._free)
+
     def used_blocks(self) -> int:
         return self._used
 
@@ -133,16 +137,19 @@ class PagedKVCacheManager:
         return pt.to(device)
 
     def commit_compaction(self, seq_ids: List[int], new_lens, freed_pages, n_freed) -> None:
-        """Apply a11s_kv_compact's results: shorter sequences, pages back on the free stack."""
+        """Apply a11s_kv_compact's results: shorter sequences, pages back on the
+        free stack in the order kv_compact lists them (the device allocator's
+        a11s_kv_release order)."""
         new_lens = torch.as_tensor(new_lens).cpu().tolist()
         n_freed = torch.as_tensor(n_freed).cpu().tolist()
         freed_pages = torch.as_tensor(freed_pages).cpu()
         for r, sid in enumerate(seq_ids):
             s = self._seqs[sid]
-            drop = set(freed_pages[r, : n_freed[r]].tolist())
+            drop = freed_pages[r, : n_freed[r]].tolist()  # a11s_kv_compact lists them in table order
             if drop:
-                s.block_table = [p for p in s.block_table if p not in drop]
-                for p in sorted(drop):
+                gone = set(drop)
+                s.block_table = [p for p in s.block_table if p not in gone]
+                for p in drop:  # pushed in that order, like free_sequence's dealloc loop
                     self._dealloc_block(p)
             self._tokens += int(new_lens[r]) - s.num_tokens
             s.num_tokens = int(new_lens[r])

@@ -201,6 +201,65 @@ def kv_compact(k_pool: torch.Tensor, v_pool: torch.Tensor, page_table: torch.Ten
     return freed_pages, n_freed
 
 
+# --------------------------------------------------------------------------- K5
+class KVPagePool:
+    """The paged KV cache's page allocator in device memory (K5): a LIFO free
+    stack of page ids with the reference PagedKVCacheManager's order
+    (src/cuda/paged_kv_cache.cu:61-149). Page tables [B][max_pages] (-1 = no
+    page) and seq_lens [B] are the caller's int32 CUDA tensors, shared with
+    tree_attention and kv_compact. Every call is asynchronous on the current
+    stream; with check_status=True it synchronises and raises A11Error for a
+    device-side error (nothing changes on an error)."""
+
+    def __init__(self, num_pages: int, device):
+        self.num_pages = int(num_pages)
+        self.free_stack = torch.empty(max(1, self.num_pages), dtype=torch.int32, device=device)
+        self.free_top = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = torch.zeros(2, dtype=torch.int32, device=device)
+        check(lib.a11s_kv_pool_init(self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_pages,
+                                    _stream()))
+
+    def _done(self, rc: int, check_status: bool) -> None:
+        check(rc)
+        if check_status:
+            code, detail = (int(x) for x in self.status.tolist())
+            if code != _lib.OK:
+                raise A11Error(code, f"device status {_lib.ERROR_NAMES.get(code, code)} (detail {detail})")
+
+    def reserve(self, page_table: torch.Tensor, seq_lens: torch.Tensor, n_new: torch.Tensor,
+                check_status: bool = False) -> None:
+        """seq_lens += n_new; tables grow to max(1, ceil(len/16)) pages (append_token / allocate_sequence)."""
+        for t, nm in ((page_table, "page_table"), (seq_lens, "seq_lens"), (n_new, "n_new")):
+            _need(t, nm, torch.int32)
+        rc = lib.a11s_kv_reserve(self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_pages,
+                                 page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(),
+                                 n_new.data_ptr(), page_table.shape[0], self.status.data_ptr(), _stream())
+        self._done(rc, check_status)
+
+    def release(self, freed_pages: torch.Tensor, n_freed: torch.Tensor, check_status: bool = False) -> None:
+        """Push the freed lists of kv_compact back on the stack (dealloc_block)."""
+        _need(freed_pages, "freed_pages", torch.int32)
+        _need(n_freed, "n_freed", torch.int32)
+        rc = lib.a11s_kv_release(self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_pages,
+                                 freed_pages.data_ptr(), freed_pages.shape[1], n_freed.data_ptr(),
+                                 freed_pages.shape[0], self.status.data_ptr(), _stream())
+        self._done(rc, check_status)
+
+    def free_sequences(self, page_table: torch.Tensor, seq_lens: torch.Tensor, mask: torch.Tensor,
+                       check_status: bool = False) -> None:
+        """Return every page of the masked sequences in table order (free_sequence)."""
+        for t, nm in ((page_table, "page_table"), (seq_lens, "seq_lens"), (mask, "mask")):
+            _need(t, nm, torch.int32)
+        rc = lib.a11s_kv_free_sequences(self.free_stack.data_ptr(), self.free_top.data_ptr(), self.num_pages,
+                                        page_table.data_ptr(), page_table.shape[1], seq_lens.data_ptr(),
+                                        mask.data_ptr(), page_table.shape[0], self.status.data_ptr(), _stream())
+        self._done(rc, check_status)
+
+    def free_pages(self) -> torch.Tensor:
+        """The stack's live entries, bottom first (a synchronising copy)."""
+        return self.free_stack[: int(self.free_top.item())].clone()
+
+
 # --------------------------------------------------------------------------- K1
 def ngram_bucket(a: int, b: int, log2_buckets: int) -> int:
     return int(lib.a11s_ngram_bucket(a, b, log2_buckets))

@@ -285,6 +285,64 @@ int a11s_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
     return A11S_OK;
 }
 
+// ------------------------------------------------------------------- K5
+int a11s_kv_pool_init(int32_t *free_stack, int32_t *free_top, int32_t num_pages, void *stream) {
+    if (num_pages < 0) return fail(A11S_EINVAL, "a11s_kv_pool_init: num_pages %d < 0", num_pages);
+    if (!free_top || (num_pages > 0 && !free_stack)) return fail(A11S_EINVAL, "a11s_kv_pool_init: null pointer");
+    cudaError_t e = a11s::launch_kv_pool_init(free_stack, free_top, num_pages, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_pool_init: launch");
+    return A11S_OK;
+}
+
+static int kv_pages_check(const char *who, int32_t *free_stack, int32_t *free_top, int32_t num_pages,
+                          int32_t batch, int32_t *status) {
+    if (num_pages < 0 || batch < 0) return fail(A11S_EINVAL, "%s: num_pages and batch must be >= 0", who);
+    if (!free_stack || !free_top || !status) return fail(A11S_EINVAL, "%s: null required pointer", who);
+    return A11S_OK;
+}
+
+int a11s_kv_reserve(int32_t *free_stack, int32_t *free_top, int32_t num_pages, int32_t *page_table,
+                    int32_t max_pages, int32_t *seq_lens, const int32_t *n_new, int32_t batch, int32_t *status,
+                    void *stream) {
+    int rc = kv_pages_check("a11s_kv_reserve", free_stack, free_top, num_pages, batch, status);
+    if (rc != A11S_OK) return rc;
+    if (max_pages < 1) return fail(A11S_EINVAL, "a11s_kv_reserve: max_pages %d < 1", max_pages);
+    if (batch > 0 && (!page_table || !seq_lens || !n_new)) return fail(A11S_EINVAL, "a11s_kv_reserve: null pointer");
+    a11s::KvPagesArgs a{free_stack, free_top, num_pages, page_table, max_pages, seq_lens, n_new, nullptr, 0,
+                        batch, status};
+    cudaError_t e = a11s::launch_kv_reserve(a, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_reserve: launch");
+    return A11S_OK;
+}
+
+int a11s_kv_release(int32_t *free_stack, int32_t *free_top, int32_t num_pages, const int32_t *freed_pages,
+                    int32_t freed_stride, const int32_t *n_freed, int32_t batch, int32_t *status, void *stream) {
+    int rc = kv_pages_check("a11s_kv_release", free_stack, free_top, num_pages, batch, status);
+    if (rc != A11S_OK) return rc;
+    if (freed_stride < 0) return fail(A11S_EINVAL, "a11s_kv_release: freed_stride %d < 0", freed_stride);
+    if (batch > 0 && (!freed_pages || !n_freed)) return fail(A11S_EINVAL, "a11s_kv_release: null pointer");
+    a11s::KvPagesArgs a{free_stack, free_top, num_pages, nullptr, 0, nullptr, n_freed, freed_pages, freed_stride,
+                        batch, status};
+    cudaError_t e = a11s::launch_kv_push(a, false, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_release: launch");
+    return A11S_OK;
+}
+
+int a11s_kv_free_sequences(int32_t *free_stack, int32_t *free_top, int32_t num_pages, int32_t *page_table,
+                           int32_t max_pages, int32_t *seq_lens, const int32_t *free_mask, int32_t batch,
+                           int32_t *status, void *stream) {
+    int rc = kv_pages_check("a11s_kv_free_sequences", free_stack, free_top, num_pages, batch, status);
+    if (rc != A11S_OK) return rc;
+    if (max_pages < 1) return fail(A11S_EINVAL, "a11s_kv_free_sequences: max_pages %d < 1", max_pages);
+    if (batch > 0 && (!page_table || !seq_lens || !free_mask))
+        return fail(A11S_EINVAL, "a11s_kv_free_sequences: null pointer");
+    a11s::KvPagesArgs a{free_stack, free_top, num_pages, page_table, max_pages, seq_lens, free_mask, nullptr, 0,
+                        batch, status};
+    cudaError_t e = a11s::launch_kv_push(a, true, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_free_sequences: launch");
+    return A11S_OK;
+}
+
 // ------------------------------------------------------------------- K2
 size_t a11s_tree_attention_workspace_bytes(int32_t batch, int32_t max_nodes, int32_t num_q_heads,
                                            int32_t num_kv_heads, int32_t head_dim,

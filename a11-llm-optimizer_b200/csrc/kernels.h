@@ -61,6 +61,22 @@ struct NgramArgs {
 
 cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s);
 
+struct KvPagesArgs {
+    int32_t *free_stack, *free_top;  // LIFO of free page ids, entries [0, *free_top)
+    int32_t num_pages;
+    int32_t *page_table;             // [B][max_pages], -1 = no page
+    int32_t max_pages;
+    int32_t *seq_lens;
+    const int32_t *counts;  // reserve: tokens to add; free: nonzero = free the sequence; release: list lengths
+    const int32_t *list;    // release: [B][list_stride] page ids
+    int32_t list_stride, B;
+    int32_t *status;        // device int32[2]: code, detail
+};
+
+cudaError_t launch_kv_pool_init(int32_t *stack, int32_t *top, int32_t n, cudaStream_t s);
+cudaError_t launch_kv_reserve(const KvPagesArgs &a, cudaStream_t s);
+cudaError_t launch_kv_push(const KvPagesArgs &a, bool whole, cudaStream_t s);
+
 struct AttnArgs {
     const void *q;
     const void *k_pool;

@@ -1,7 +1,7 @@
 /*
  * a11spec.h - C ABI of the B200 speculative-decoding hot path.
  *
- * Four device steps, one entry point each, all asynchronous on the caller's
+ * Five device steps, all asynchronous on the caller's
  * CUDA stream (passed as `void *stream`, a cudaStream_t; NULL = legacy
  * default stream):
  *
@@ -9,6 +9,8 @@
  *   a11s_tree_attention   tree-masked attention over 16-token KV pages   (K2)
  *   a11s_accept           vocab softmax/argmax + acceptance + bonus draw  (K3)
  *   a11s_kv_compact       move the accepted path's KV, shrink page tables (K4)
+ *   a11s_kv_reserve / a11s_kv_release / a11s_kv_free_sequences
+ *                         the page allocator of the paged KV cache    (K5)
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are caller-owned DEVICE pointers, row-major and
@@ -231,6 +233,60 @@ int a11s_kv_compact(void *k_pool, void *v_pool, int32_t num_layers, int64_t laye
                     const int32_t *n_nodes, int32_t batch, int32_t max_nodes,
                     int32_t *freed_pages, int32_t *n_freed, void *workspace,
                     size_t workspace_bytes, void *stream);
+
+/* ------------------------------------------------------------------------ K5
+ * The page allocator of the paged KV cache on the device. Replaces
+ * PagedKVCacheManager's host bookkeeping (src/cuda/paged_kv_cache.cu:
+ * init_pool 61-81, alloc_block 85-93, dealloc_block 95-101, allocate_sequence
+ * 103-117, append_token 119-135, free_sequence 137-149; kv_cache.py:131-156)
+ * so a decode step grows and returns pages without a host round trip.
+ *
+ * State in device memory: free_stack int32[num_pages] (a LIFO of free page
+ * ids, entries [0, *free_top)), free_top int32[1], page_table
+ * int32[batch][max_pages] (-1 = no page) and seq_lens int32[batch].
+ * Invariant kept by these calls and a11s_kv_compact: an active sequence of
+ * length len owns table entries 0 .. max(1, ceil(len/16)) - 1 and has -1
+ * after them; an inactive one has -1 everywhere.
+ *
+ * Each call serves the whole batch in batch order and, within a sequence, in
+ * logical page order, exactly like the reference's per-token loop. It checks
+ * everything first and changes nothing on an error, which it writes to
+ * `status` (device int32[2]: code, detail = offending sequence or count);
+ * A11S_OK there otherwise. Calls on one pool must not overlap on the GPU (use
+ * one stream): they race.
+ *
+ *   a11s_kv_pool_init      free_stack[i] = i, *free_top = num_pages: the
+ *                          reference's initial order, so the highest id is
+ *                          taken first.
+ *   a11s_kv_reserve        seq_lens[b] += n_new[b] and the sequence's table
+ *                          grows to max(1, ceil(len/16)) pages popped from
+ *                          the stack (an inactive sequence gets its first
+ *                          page, even with n_new[b] == 0: allocate_sequence).
+ *                          Errors: A11S_ENOSPACE when the stack holds fewer
+ *                          pages than the batch needs (the reference's "out
+ *                          of physical blocks"), A11S_EBOUNDS when a table
+ *                          row would exceed max_pages or a count is negative.
+ *   a11s_kv_release        pushes freed_pages[b][0 .. n_freed[b]) (the lists
+ *                          a11s_kv_compact produces; freed_stride entries per
+ *                          row) back on the stack. A11S_EBOUNDS for ids
+ *                          outside the pool or a stack overflow (double free).
+ *   a11s_kv_free_sequences for every b with free_mask[b] != 0 and an active
+ *                          table: pushes its pages in table order, clears the
+ *                          row to -1 and sets seq_lens[b] = 0 (free_sequence).
+ */
+int a11s_kv_pool_init(int32_t *free_stack, int32_t *free_top, int32_t num_pages, void *stream);
+
+int a11s_kv_reserve(int32_t *free_stack, int32_t *free_top, int32_t num_pages, int32_t *page_table,
+                    int32_t max_pages, int32_t *seq_lens, const int32_t *n_new, int32_t batch,
+                    int32_t *status, void *stream);
+
+int a11s_kv_release(int32_t *free_stack, int32_t *free_top, int32_t num_pages, const int32_t *freed_pages,
+                    int32_t freed_stride, const int32_t *n_freed, int32_t batch, int32_t *status,
+                    void *stream);
+
+int a11s_kv_free_sequences(int32_t *free_stack, int32_t *free_top, int32_t num_pages, int32_t *page_table,
+                           int32_t max_pages, int32_t *seq_lens, const int32_t *free_mask, int32_t batch,
+                           int32_t *status, void *stream);
 
 /* ------------------------------------------------------------------------ K1
  * Hashed trigram drafting into a token tree. Replaces

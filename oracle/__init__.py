@@ -8,7 +8,8 @@ package and ``liba11spec.so``) never does.
 * ``liba11oracle.so`` (built from ``a11oracle.c`` by ``Makefile``) restates the
   path in plain C: acceptance (rule of the reference's
   src/engine/speculative_verifier.cpp:102-132), the chunked fixed-point
-  softmax, tree attention (engine/pipeline.py:386-402), compaction and n-gram
+  softmax, tree attention (engine/pipeline.py:386-402), compaction, the
+  paged-KV page allocator (src/cuda/paged_kv_cache.cu:85-149) and n-gram
   expansion.
 * ``_ref/libref_verifier.so`` (``make ref``, only where the reference tree is
   mounted) is the reference's own ``SpeculativeTreeVerifier`` behind the
@@ -76,6 +77,11 @@ def lib():
         L.or_kv_compact.argtypes = [_u8p, _u8p, C.c_int32, C.c_int64, C.c_int32, C.c_int32,
                                     C.c_int32, _i32p, C.c_int32, _i32p, _i32p, _i32p, C.c_void_p,
                                     C.c_int32, C.c_int32, _i32p, _i32p]
+        L.or_kv_reserve.argtypes = [_i32p, _i32p, C.c_int32, _i32p, C.c_int32, _i32p, _i32p, C.c_int32,
+                                    _i32p]
+        L.or_kv_release.argtypes = [_i32p, _i32p, C.c_int32, _i32p, C.c_int32, _i32p, C.c_int32, _i32p]
+        L.or_kv_free_sequences.argtypes = [_i32p, _i32p, C.c_int32, _i32p, C.c_int32, _i32p, _i32p,
+                                           C.c_int32, _i32p]
         L.or_ngram_bucket.restype = C.c_uint32
         L.or_ngram_bucket.argtypes = [C.c_int32, C.c_int32, C.c_int32]
         L.or_ngram_expand.argtypes = [_i32p, C.c_int32, C.c_int32, _i32p, C.c_int32, C.c_int32,
@@ -199,6 +205,46 @@ def kv_compact(k_pool: np.ndarray, v_pool: np.ndarray, page_table, seq_lens, acc
                              N, freed, nfreed)
     return dict(k_pool=kb, v_pool=vb, page_table=pt, seq_lens=sl, freed_pages=freed,
                 n_freed=nfreed, status=rc)
+
+
+# ----------------------------------------------------------------------------- page allocator
+def _pool_state(stack, top, num_pages):
+    st = np.zeros(max(1, num_pages), np.int32)
+    st[: len(stack)] = np.asarray(stack, dtype=np.int32)
+    return st, np.array([top], np.int32)
+
+
+def kv_reserve(stack, top, num_pages, page_table, seq_lens, n_new):
+    """PagedKVCacheManager allocate_sequence / append_token over a batch, on copies.
+    stack: the live entries (bottom first); returns the new state and (status, detail)."""
+    st, tp = _pool_state(stack, top, num_pages)
+    pt = np.ascontiguousarray(page_table, dtype=np.int32).copy()
+    sl = np.ascontiguousarray(seq_lens, dtype=np.int32).copy()
+    det = np.zeros(1, np.int32)
+    rc = lib().or_kv_reserve(st, tp, num_pages, pt, pt.shape[1], sl, np.ascontiguousarray(n_new, dtype=np.int32),
+                             pt.shape[0], det)
+    return dict(stack=st[: tp[0]].copy(), top=int(tp[0]), page_table=pt, seq_lens=sl, status=rc, detail=int(det[0]))
+
+
+def kv_release(stack, top, num_pages, freed_pages, n_freed):
+    """dealloc_block of each freed list, batch order, on copies."""
+    st, tp = _pool_state(stack, top, num_pages)
+    fp = np.ascontiguousarray(freed_pages, dtype=np.int32)
+    det = np.zeros(1, np.int32)
+    rc = lib().or_kv_release(st, tp, num_pages, fp, fp.shape[1], np.ascontiguousarray(n_freed, dtype=np.int32),
+                             fp.shape[0], det)
+    return dict(stack=st[: tp[0]].copy(), top=int(tp[0]), status=rc, detail=int(det[0]))
+
+
+def kv_free_sequences(stack, top, num_pages, page_table, seq_lens, mask):
+    """free_sequence of every masked sequence, batch order, on copies."""
+    st, tp = _pool_state(stack, top, num_pages)
+    pt = np.ascontiguousarray(page_table, dtype=np.int32).copy()
+    sl = np.ascontiguousarray(seq_lens, dtype=np.int32).copy()
+    det = np.zeros(1, np.int32)
+    rc = lib().or_kv_free_sequences(st, tp, num_pages, pt, pt.shape[1], sl, np.ascontiguousarray(mask, dtype=np.int32),
+                                    pt.shape[0], det)
+    return dict(stack=st[: tp[0]].copy(), top=int(tp[0]), page_table=pt, seq_lens=sl, status=rc, detail=int(det[0]))
 
 
 # ----------------------------------------------------------------------------- n-gram

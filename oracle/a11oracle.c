@@ -664,3 +664,104 @@ int or_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
     }
     return ST_OK;
 }
+
+/* ------------------------------------------------------------------------
+ * Page allocator of the paged KV cache, restated from the reference's
+ * PagedKVCacheManager (src/cuda/paged_kv_cache.cu): alloc_block 85-93 pops the
+ * back of the free stack, append_token 119-135 adds a block when the token
+ * count exceeds blocks * 16, allocate_sequence 103-117 gives a new sequence
+ * one block, dealloc_block 95-101 / free_sequence 137-149 push blocks back in
+ * block-table order. The stack is stack[0 .. *top); the batch is served in
+ * order, token by token. Unlike the reference, a batch that cannot be served
+ * changes nothing (checked before the loop) and reports a code and a detail:
+ * EBOUNDS + the lowest offending sequence, EBOUNDS + -1 for a stack that
+ * would leave [0, num_pages], ENOSPACE + the pages the batch needs.
+ * ------------------------------------------------------------------------ */
+#define ST_ENOSPACE 6
+
+static int32_t or_blocks_for(int32_t len) { return len <= 0 ? 1 : (len + 15) / 16; }
+
+int or_kv_reserve(int32_t *stack, int32_t *top, int32_t num_pages, int32_t *page_table, int32_t max_pages,
+                  int32_t *seq_lens, const int32_t *n_new, int32_t batch, int32_t *detail) {
+    long long need = 0;
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t len = seq_lens[b], add = n_new[b];
+        const int active = page_table[(size_t)b * max_pages] >= 0;
+        if (len < 0 || add < 0 || (long long)len + add > 2147483647LL || (!active && len != 0) ||
+            or_blocks_for(len + add) > max_pages) {
+            *detail = b;
+            return ST_EBOUNDS;
+        }
+        need += or_blocks_for(len + add) - (active ? or_blocks_for(len) : 0);
+    }
+    if (*top < 0 || *top > num_pages) { *detail = -1; return ST_EBOUNDS; }
+    if (need > *top) { *detail = need > 2147483647LL ? 2147483647 : (int32_t)need; return ST_ENOSPACE; }
+    for (int32_t b = 0; b < batch; ++b) {
+        int32_t *row = page_table + (size_t)b * max_pages;
+        int32_t blocks;
+        if (row[0] < 0) {  /* allocate_sequence: the first block */
+            row[0] = stack[--*top];
+            blocks = 1;
+        } else {
+            blocks = or_blocks_for(seq_lens[b]);
+        }
+        for (int32_t t = 0; t < n_new[b]; ++t) {  /* append_token */
+            seq_lens[b] += 1;
+            if (seq_lens[b] > blocks * 16) row[blocks++] = stack[--*top];
+        }
+    }
+    *detail = 0;
+    return ST_OK;
+}
+
+static int or_kv_push(int32_t *stack, int32_t *top, int32_t num_pages, int32_t *page_table, int32_t max_pages,
+                      int32_t *seq_lens, const int32_t *counts, const int32_t *list, int32_t list_stride,
+                      int32_t batch, int whole, int32_t *detail) {
+    long long total = 0;
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t *src;
+        int32_t n;
+        if (whole) {
+            src = page_table + (size_t)b * max_pages;
+            if (!counts[b] || src[0] < 0) continue;
+            if (seq_lens[b] < 0) { *detail = b; return ST_EBOUNDS; }
+            n = or_blocks_for(seq_lens[b]);
+            if (n > max_pages) n = max_pages;
+        } else {
+            src = list + (size_t)b * list_stride;
+            n = counts[b];
+            if (n < 0 || n > list_stride) { *detail = b; return ST_EBOUNDS; }
+        }
+        for (int32_t j = 0; j < n; ++j)
+            if (src[j] < 0 || src[j] >= num_pages) { *detail = b; return ST_EBOUNDS; }
+        total += n;
+    }
+    if (*top < 0 || *top + total > num_pages) { *detail = -1; return ST_EBOUNDS; }
+    for (int32_t b = 0; b < batch; ++b) {
+        if (whole) {
+            int32_t *row = page_table + (size_t)b * max_pages;
+            if (!counts[b] || row[0] < 0) continue;
+            int32_t n = or_blocks_for(seq_lens[b]);
+            if (n > max_pages) n = max_pages;
+            for (int32_t j = 0; j < n; ++j) {  /* free_sequence: dealloc in table order */
+                stack[(*top)++] = row[j];
+                row[j] = -1;
+            }
+            seq_lens[b] = 0;
+        } else {
+            for (int32_t j = 0; j < counts[b]; ++j) stack[(*top)++] = list[(size_t)b * list_stride + j];
+        }
+    }
+    *detail = 0;
+    return ST_OK;
+}
+
+int or_kv_release(int32_t *stack, int32_t *top, int32_t num_pages, const int32_t *freed_pages,
+                  int32_t freed_stride, const int32_t *n_freed, int32_t batch, int32_t *detail) {
+    return or_kv_push(stack, top, num_pages, NULL, 0, NULL, n_freed, freed_pages, freed_stride, batch, 0, detail);
+}
+
+int or_kv_free_sequences(int32_t *stack, int32_t *top, int32_t num_pages, int32_t *page_table, int32_t max_pages,
+                         int32_t *seq_lens, const int32_t *free_mask, int32_t batch, int32_t *detail) {
+    return or_kv_push(stack, top, num_pages, page_table, max_pages, seq_lens, free_mask, NULL, 0, batch, 1, detail);
+}

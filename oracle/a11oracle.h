@@ -58,6 +58,14 @@ int or_kv_compact(uint8_t *k_pool, uint8_t *v_pool, int32_t num_layers, int64_t 
                   const int32_t *accepted_nodes, const int32_t *n_nodes, int32_t batch,
                   int32_t max_nodes, int32_t *freed_pages, int32_t *n_freed);
 
+/* Page allocator of the paged KV cache (src/cuda/paged_kv_cache.cu:85-149). */
+int or_kv_reserve(int32_t *stack, int32_t *top, int32_t num_pages, int32_t *page_table, int32_t max_pages,
+                  int32_t *seq_lens, const int32_t *n_new, int32_t batch, int32_t *detail);
+int or_kv_release(int32_t *stack, int32_t *top, int32_t num_pages, const int32_t *freed_pages,
+                  int32_t freed_stride, const int32_t *n_freed, int32_t batch, int32_t *detail);
+int or_kv_free_sequences(int32_t *stack, int32_t *top, int32_t num_pages, int32_t *page_table, int32_t max_pages,
+                         int32_t *seq_lens, const int32_t *free_mask, int32_t batch, int32_t *detail);
+
 uint32_t or_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets);
 int or_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
                     const int32_t *last_tokens, int32_t batch, int32_t width_root,

@@ -1,0 +1,138 @@
+"""The paged-KV page allocator (K5) on the GPU against the oracle, bit-exact:
+free stack, stack top, page tables, lengths and status, through whole
+decode-step lifecycles (reserve tree slots -> a11s_kv_compact -> release the
+freed pages -> free finished sequences), a batch larger than one block of
+threads, and the all-or-nothing error cases."""
+import numpy as np
+import pytest
+import torch
+
+import a11spec
+import oracle
+from a11spec.ops import KVPagePool
+
+pytestmark = pytest.mark.gpu
+
+OK, EBOUNDS, ENOSPACE = 0, 2, 6
+
+
+def _state(pool, pt, sl):
+    torch.cuda.synchronize()
+    return (pool.free_pages().cpu().numpy(), int(pool.free_top.item()), pt.cpu().numpy(), sl.cpu().numpy(),
+            [int(x) for x in pool.status.tolist()])
+
+
+def _same(dev, ref, what):
+    stack, top, pt, sl, st = dev
+    assert st[0] == ref["status"] and st[1] == ref["detail"], (what, st, ref["status"], ref["detail"])
+    assert top == ref["top"], what
+    np.testing.assert_array_equal(stack, ref["stack"], err_msg=what)
+    if "page_table" in ref:
+        np.testing.assert_array_equal(pt, ref["page_table"], err_msg=what)
+        np.testing.assert_array_equal(sl, ref["seq_lens"], err_msg=what)
+
+
+def test_decode_step_lifecycle_matches_oracle(dev):
+    rng = np.random.default_rng(11)
+    B, N, MP, P, Hkv, D = 6, 24, 32, 120, 2, 16
+    pool = KVPagePool(P, dev)
+    pt = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+    sl = torch.zeros(B, dtype=torch.int32, device=dev)
+    k_pool = torch.randn(P, 16, Hkv, D, device=dev).to(torch.bfloat16)
+    v_pool = torch.randn(P, 16, Hkv, D, device=dev).to(torch.bfloat16)
+    o_stack, o_top = list(range(P)), P
+    o_pt, o_sl = pt.cpu().numpy(), sl.cpu().numpy()
+    o_k, o_v = k_pool.cpu().view(torch.int16).numpy(), v_pool.cpu().view(torch.int16).numpy()
+    # prompts of random length
+    prompt = rng.integers(1, 60, B).astype(np.int32)
+    pool.reserve(pt, sl, torch.from_numpy(prompt).to(dev))
+    ref = oracle.kv_reserve(o_stack, o_top, P, o_pt, o_sl, prompt)
+    _same(_state(pool, pt, sl), ref, "prompt")
+    o_stack, o_top, o_pt, o_sl = list(ref["stack"]), ref["top"], ref["page_table"], ref["seq_lens"]
+    for step in range(8):
+        n_nodes = rng.integers(1, N + 1, B).astype(np.int32)
+        ctx = o_sl.copy()
+        pool.reserve(pt, sl, torch.from_numpy(n_nodes).to(dev))  # tree slots
+        ref = oracle.kv_reserve(o_stack, o_top, P, o_pt, o_sl, n_nodes)
+        _same(_state(pool, pt, sl), ref, f"tree slots {step}")
+        o_stack, o_top, o_pt = list(ref["stack"]), ref["top"], ref["page_table"]
+        # accepted path: a chain of distinct increasing nodes, shorter than the tree
+        alen = np.array([rng.integers(0, n) for n in n_nodes], np.int32)
+        acc = np.full((B, N), -1, np.int32)
+        for b in range(B):
+            acc[b, : alen[b]] = np.sort(rng.choice(np.arange(1, n_nodes[b]), alen[b], replace=False))
+        sl.copy_(torch.from_numpy(ctx))  # kv_compact takes the length before the tree
+        freed, nfreed = a11spec.kv_compact(k_pool, v_pool, pt, sl, torch.from_numpy(alen).to(dev),
+                                           torch.from_numpy(acc).to(dev), torch.from_numpy(n_nodes).to(dev),
+                                           check_status=True)
+        rc = oracle.kv_compact(o_k, o_v, o_pt, ctx, alen, acc, n_nodes)
+        o_k, o_v, o_pt, o_sl = rc["k_pool"], rc["v_pool"], rc["page_table"], rc["seq_lens"]
+        np.testing.assert_array_equal(freed.cpu().numpy(), rc["freed_pages"])
+        pool.release(freed, nfreed)
+        ref = oracle.kv_release(o_stack, o_top, P, rc["freed_pages"], rc["n_freed"])
+        _same(_state(pool, pt, sl), ref, f"release {step}")
+        o_stack, o_top = list(ref["stack"]), ref["top"]
+        np.testing.assert_array_equal(pt.cpu().numpy(), o_pt)
+        np.testing.assert_array_equal(sl.cpu().numpy(), o_sl)
+        if step % 3 == 2:  # a finished request leaves and a new one arrives
+            mask = np.zeros(B, np.int32)
+            mask[rng.integers(0, B)] = 1
+            pool.free_sequences(pt, sl, torch.from_numpy(mask).to(dev))
+            ref = oracle.kv_free_sequences(o_stack, o_top, P, o_pt, o_sl, mask)
+            _same(_state(pool, pt, sl), ref, f"free {step}")
+            o_stack, o_top, o_pt, o_sl = list(ref["stack"]), ref["top"], ref["page_table"], ref["seq_lens"]
+            new = (mask * rng.integers(1, 40)).astype(np.int32)
+            pool.reserve(pt, sl, torch.from_numpy(new).to(dev))
+            ref = oracle.kv_reserve(o_stack, o_top, P, o_pt, o_sl, new)
+            _same(_state(pool, pt, sl), ref, f"new request {step}")
+            o_stack, o_top, o_pt, o_sl = list(ref["stack"]), ref["top"], ref["page_table"], ref["seq_lens"]
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(k_pool.cpu().view(torch.int16).numpy(), o_k)
+
+
+def test_large_batch_multi_tile(dev):
+    rng = np.random.default_rng(3)
+    B, MP, P = 3000, 8, 30000
+    pool = KVPagePool(P, dev)
+    pt = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+    sl = torch.zeros(B, dtype=torch.int32, device=dev)
+    o = dict(stack=list(range(P)), top=P, page_table=pt.cpu().numpy(), seq_lens=sl.cpu().numpy())
+    for r in range(3):
+        n_new = rng.integers(0, 40, B).astype(np.int32)
+        pool.reserve(pt, sl, torch.from_numpy(n_new).to(dev))
+        ref = oracle.kv_reserve(o["stack"], o["top"], P, o["page_table"], o["seq_lens"], n_new)
+        _same(_state(pool, pt, sl), ref, f"reserve {r}")
+        o = ref
+        mask = (rng.random(B) < 0.25).astype(np.int32)
+        pool.free_sequences(pt, sl, torch.from_numpy(mask).to(dev))
+        ref = oracle.kv_free_sequences(o["stack"], o["top"], P, o["page_table"], o["seq_lens"], mask)
+        _same(_state(pool, pt, sl), ref, f"free {r}")
+        o = ref
+
+
+def test_errors_change_nothing_and_match_oracle(dev):
+    P = 10
+    pool = KVPagePool(P, dev)
+    pt = torch.full((3, 8), -1, dtype=torch.int32, device=dev)
+    sl = torch.zeros(3, dtype=torch.int32, device=dev)
+    n_new = np.array([40, 40, 40], np.int32)  # 9 pages of 10: fits
+    pool.reserve(pt, sl, torch.from_numpy(n_new).to(dev), check_status=True)
+    before = _state(pool, pt, sl)
+    more = np.array([40, 0, 0], np.int32)  # sequence 0 needs 2 more pages, 1 is left
+    with pytest.raises(a11spec.A11Error):
+        pool.reserve(pt, sl, torch.from_numpy(more).to(dev), check_status=True)
+    after = _state(pool, pt, sl)
+    ref = oracle.kv_reserve(before[0], before[1], P, before[2], before[3], more)
+    assert ref["status"] == ENOSPACE
+    _same(after, ref, "enospace")
+    for a, b in zip(before[:4], after[:4]):
+        np.testing.assert_array_equal(np.asarray(a), np.asarray(b))
+    big = np.array([0, 100, 0], np.int32)  # 140 tokens need 9 > 8 pages: EBOUNDS at sequence 1
+    pool.reserve(pt, sl, torch.from_numpy(big).to(dev))
+    ref = oracle.kv_reserve(before[0], before[1], P, before[2], before[3], big)
+    assert ref["status"] == EBOUNDS and ref["detail"] == 1
+    _same(_state(pool, pt, sl), ref, "ebounds")
+    lists = torch.tensor([[3, 99]], dtype=torch.int32, device=dev)  # page 99 outside the pool
+    pool.release(lists, torch.tensor([2], dtype=torch.int32, device=dev))
+    st = _state(pool, pt, sl)
+    assert st[4] == [EBOUNDS, 0] and st[1] == before[1]
