@@ -121,17 +121,33 @@ class SpeculativeDecoder:
     def step(self, last_tokens: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
              page_table: torch.Tensor, seq_lens: torch.Tensor,
              logits_fn: Callable[[torch.Tensor, DraftTree], torch.Tensor],
-             uniforms: Optional[torch.Tensor] = None):
+             uniforms: Optional[torch.Tensor] = None, pages: Optional["ops.KVPagePool"] = None,
+             kv_fn: Optional[Callable[[DraftTree, torch.Tensor, torch.Tensor], None]] = None):
         """One speculative step on the device: draft (K1), tree attention (K2),
         logits_fn(attention_out, tree) -> [B, N, V] (the target model's
         remaining layers and LM head), acceptance (K3), compaction (K4).
-        The tree's K/V must already sit at positions seq_lens + i of the pools.
-        Returns (tree, acceptance result); seq_lens/page_table are updated."""
+
+        Without `pages` the caller has already given the tree slots (positions
+        seq_lens + i) their pages. With a KVPagePool the step reserves exactly
+        the drafted tree's slots after drafting (K5) and returns the pages
+        compaction detaches, so page tables, lengths and the free stack stay
+        on the device. `kv_fn(tree, page_table, seq_lens)`, when given, runs
+        between the reservation and the attention: the target model writes the
+        tree's K/V there. Returns (tree, acceptance result); seq_lens and
+        page_table are updated."""
         tree = self.draft(last_tokens)
+        if pages is not None:
+            grown = seq_lens.clone()
+            pages.reserve(page_table, grown, tree.n_nodes)
+        if kv_fn is not None:
+            kv_fn(tree, page_table, seq_lens)
         attn, _, _ = ops.tree_attention(q, k_pool, v_pool, page_table, seq_lens, tree.parents, tree.n_nodes)
         logits = logits_fn(attn, tree)
         res = self.verify(tree, logits, uniforms=uniforms)
-        ops.kv_compact(k_pool, v_pool, page_table, seq_lens, res.accept_len, res.accepted_nodes, tree.n_nodes)
+        freed, n_freed = ops.kv_compact(k_pool, v_pool, page_table, seq_lens, res.accept_len, res.accepted_nodes,
+                                        tree.n_nodes)
+        if pages is not None:
+            pages.release(freed, n_freed)
         return tree, res
 
     def diagnostics(self) -> dict:

@@ -136,3 +136,37 @@ def test_errors_change_nothing_and_match_oracle(dev):
     pool.release(lists, torch.tensor([2], dtype=torch.int32, device=dev))
     st = _state(pool, pt, sl)
     assert st[4] == [EBOUNDS, 0] and st[1] == before[1]
+
+
+def test_decoder_steps_keep_pages_on_device(dev):
+    """SpeculativeDecoder.step with a KVPagePool: tree slots reserved after
+    drafting, detached pages returned after compaction; after each step every
+    table holds exactly max(1, ceil(len/16)) pages and the stack the rest."""
+    from a11spec.decoder import SpeculativeDecoder
+    from a11spec import workloads as W
+    V, B, N, Hkv, Hq, D, MP, P = 4096, 3, 16, 2, 16, 128, 16, 64
+    table = W.make_ngram_table(log2_buckets=10, vocab=V, seed=2)
+    dec = SpeculativeDecoder(table=torch.from_numpy(table), log2_buckets=10, max_depth=3, max_nodes=N,
+                             temperature=0.7)
+    pool = KVPagePool(P, dev)
+    kpool = torch.randn(P, 16, Hkv, D, device=dev).to(torch.bfloat16)
+    vpool = torch.randn(P, 16, Hkv, D, device=dev).to(torch.bfloat16)
+    pt = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+    lens = torch.zeros(B, dtype=torch.int32, device=dev)
+    pool.reserve(pt, lens, torch.tensor([40, 77, 5], dtype=torch.int32, device=dev), check_status=True)
+    last = torch.tensor([[5, 9], [1, 2], [7, 7]], dtype=torch.int32, device=dev)
+    for step in range(4):
+        before = lens.cpu().clone()
+        q = torch.randn(B, N, Hq, D, device=dev).to(torch.bfloat16)
+        tree, res = dec.step(last, q, kpool, vpool, pt, lens,
+                             lambda attn, tr: torch.randn(B, N, V, device=dev).to(torch.bfloat16), pages=pool)
+        torch.cuda.synchronize()
+        assert int(pool.status[0]) == OK, pool.status.tolist()
+        assert torch.equal(lens.cpu(), before + 1 + res.accept_len.cpu())
+        held = (pt >= 0).sum(dim=1).cpu()
+        want = torch.clamp((lens.cpu() + 15) // 16, min=1)
+        assert torch.equal(held, want.to(held.dtype)), (step, held, want)
+        assert int(pool.free_top.item()) == P - int(want.sum())
+        used = set(pt[pt >= 0].cpu().tolist())
+        assert used.isdisjoint(set(pool.free_pages().cpu().tolist())) and len(used) == int(want.sum())
+        last = torch.stack([last[:, 1], res.bonus.clamp_min(0)], dim=1).contiguous()
