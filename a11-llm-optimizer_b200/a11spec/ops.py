@@ -1,4 +1,4 @@
-"""Torch-facing wrappers of the four C-ABI entry points.
+"""Torch-facing wrappers of the C-ABI entry points.
 
 Every function takes CUDA tensors, launches on the current torch stream and
 returns without synchronising (unless ``check_status=True``, which reads the
@@ -258,6 +258,47 @@ class KVPagePool:
     def free_pages(self) -> torch.Tensor:
         """The stack's live entries, bottom first (a synchronising copy)."""
         return self.free_stack[: int(self.free_top.item())].clone()
+
+
+# --------------------------------------------------------------------------- K6
+def history_from_accept(last_tokens: torch.Tensor, accepted_tokens: torch.Tensor, accept_len: torch.Tensor,
+                        bonus: torch.Tensor):
+    """History rows of one acceptance step for ngram_update: (last_tokens[b][0],
+    last_tokens[b][1], accepted_tokens[b][0 .. accept_len[b]), bonus[b]) and
+    their lengths, built with device ops (no host synchronisation)."""
+    B, N = accepted_tokens.shape
+    hist = torch.full((B, N + 3), -1, dtype=torch.int32, device=accepted_tokens.device)
+    hist[:, :2] = last_tokens
+    hist[:, 2:2 + N] = accepted_tokens
+    alen = accept_len.long().clamp(0, N)
+    hist.scatter_(1, (2 + alen).unsqueeze(1), bonus.to(torch.int32).unsqueeze(1))
+    lens = (alen + 3).to(torch.int32)
+    return hist, lens
+
+
+def ngram_update(table: torch.Tensor, history: torch.Tensor, lens: torch.Tensor, log2_buckets: int,
+                 status: Optional[torch.Tensor] = None, check_status: bool = False) -> torch.Tensor:
+    """K6, in place on table int32 [2^k, slots, 2]: adds the trigrams of each
+    history row (rows split into calls of at most NGRAM_MAX_UPDATES trigrams).
+    Returns the device status int32[2] of the last call."""
+    _need(table, "table", torch.int32)
+    _need(history, "history", torch.int32)
+    _need(lens, "lens", torch.int32)
+    if status is None:
+        status = torch.zeros(2, dtype=torch.int32, device=table.device)
+    B, stride = history.shape
+    per = max(1, _lib.NGRAM_MAX_UPDATES // max(1, stride - 2))
+    for b0 in range(0, max(B, 1), per):
+        rows = history[b0:b0 + per]
+        rc = lib.a11s_ngram_update(table.data_ptr(), log2_buckets, table.shape[1], _ptr(rows) if B else None,
+                                   stride, _ptr(lens[b0:b0 + per]) if B else None, rows.shape[0],
+                                   status.data_ptr(), _stream())
+        check(rc)
+        if check_status:
+            code, detail = (int(x) for x in status.tolist())
+            if code != _lib.OK:
+                raise A11Error(code, f"device status {_lib.ERROR_NAMES.get(code, code)} (row {b0 + detail})")
+    return status
 
 
 # --------------------------------------------------------------------------- K1

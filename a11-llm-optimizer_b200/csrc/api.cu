@@ -285,6 +285,27 @@ int a11s_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
     return A11S_OK;
 }
 
+int a11s_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const int32_t *history,
+                      int32_t history_stride, const int32_t *history_len, int32_t batch, int32_t *status,
+                      void *stream) {
+    if (log2_buckets < 1 || log2_buckets > 30)
+        return fail(A11S_EINVAL, "a11s_ngram_update: log2_buckets %d outside [1, 30]", log2_buckets);
+    if (slots < 1 || slots > 32) return fail(A11S_EUNSUPPORTED, "a11s_ngram_update: slots %d outside [1, 32]", slots);
+    if (batch < 0 || history_stride < 0) return fail(A11S_EINVAL, "a11s_ngram_update: batch and stride must be >= 0");
+    const long long updates = (long long)batch * (history_stride > 2 ? history_stride - 2 : 0);
+    if (updates > A11S_NGRAM_MAX_UPDATES)
+        return fail(A11S_EUNSUPPORTED, "a11s_ngram_update: batch * (stride - 2) = %lld > %d trigrams per call",
+                    updates, A11S_NGRAM_MAX_UPDATES);
+    if (!table || !status || (batch > 0 && (!history || !history_len)))
+        return fail(A11S_EINVAL, "a11s_ngram_update: null required pointer");
+    int cap = 1;
+    while (cap < updates) cap <<= 1;
+    a11s::NgramUpdateArgs a{table, log2_buckets, slots, history, history_len, batch, history_stride, cap, status};
+    cudaError_t e = a11s::launch_ngram_update(a, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_ngram_update: launch");
+    return A11S_OK;
+}
+
 // ------------------------------------------------------------------- K5
 int a11s_kv_pool_init(int32_t *free_stack, int32_t *free_top, int32_t num_pages, void *stream) {
     if (num_pages < 0) return fail(A11S_EINVAL, "a11s_kv_pool_init: num_pages %d < 0", num_pages);

@@ -61,6 +61,18 @@ struct NgramArgs {
 
 cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s);
 
+struct NgramUpdateArgs {
+    int32_t *table;
+    int32_t log2_buckets, slots;
+    const int32_t *history;  // [B][stride]
+    const int32_t *lens;
+    int32_t B, stride;
+    int32_t cap;             // shared-memory keys: a power of two >= B * max(0, stride - 2)
+    int32_t *status;
+};
+
+cudaError_t launch_ngram_update(const NgramUpdateArgs &a, cudaStream_t s);
+
 struct KvPagesArgs {
     int32_t *free_stack, *free_top;  // LIFO of free page ids, entries [0, *free_top)
     int32_t num_pages;

@@ -86,4 +86,123 @@ cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// K6: the table learns the trigrams of committed tokens.
+//
+// Every history row b contributes the trigrams (h[i-2], h[i-1], h[i]) for
+// 2 <= i < len[b] whose three tokens are >= 0. A trigram (x, y, z) updates
+// bucket(x, y): the slot holding z with a positive count gains 1 (saturating);
+// else the lowest slot with count <= 0 becomes (z, 1); else the slot with the
+// smallest count (lowest index among equals) is replaced by (z, 1). Updates
+// of one bucket apply in (row, position) order; buckets are independent.
+//
+// One block: the updates' keys (bucket << 32 | history index) go to shared
+// memory, a bitonic sort orders them, and the first thread of each bucket's
+// run applies that run in order. So the result equals the serial loop over
+// rows and positions, whatever the contention on a bucket.
+// ---------------------------------------------------------------------------
+constexpr int kUpdThreads = 1024;
+
+__global__ void __launch_bounds__(kUpdThreads, 1) ngram_update_kernel(const NgramUpdateArgs a) {
+    extern __shared__ unsigned long long keys[];  // a.cap entries
+    __shared__ int ws[kUpdThreads / 32 + 1];
+    __shared__ int s_bad;
+    if (threadIdx.x == 0) s_bad = INT32_MAX;
+    __syncthreads();
+    // validate the lengths first: nothing changes on an error
+    for (int b = threadIdx.x; b < a.B; b += blockDim.x) {
+        const int n = a.lens[b];
+        if (n < 0 || n > a.stride) atomicMin(&s_bad, b);
+    }
+    __syncthreads();
+    if (s_bad != INT32_MAX) {
+        if (threadIdx.x == 0) { a.status[0] = A11S_EBOUNDS; a.status[1] = s_bad; }
+        return;
+    }
+    // gather the keys: a row's trigram slots in order, rows in order
+    __shared__ int s_total;
+    if (threadIdx.x == 0) s_total = 0;
+    __syncthreads();
+    for (int b = 0; b < a.B; ++b) {  // rows are few: one pass per row, all threads over its positions
+        const int n = a.lens[b];
+        const int32_t *h = a.history + (size_t)b * a.stride;
+        const int base = s_total;
+        int cnt = 0;
+        for (int i0 = 2; i0 < n; i0 += blockDim.x) {
+            const int i = i0 + threadIdx.x;
+            const bool ok = i < n && h[i - 2] >= 0 && h[i - 1] >= 0 && h[i] >= 0;
+            // block-wide compaction of the valid positions, order kept
+            const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+            const unsigned m = __ballot_sync(0xffffffffu, ok);
+            if (lane == 0) ws[warp] = __popc(m);
+            __syncthreads();
+            if (threadIdx.x == 0) {
+                int acc = 0;
+                for (int w = 0; w < (int)(blockDim.x / 32); ++w) { const int t = ws[w]; ws[w] = acc; acc += t; }
+                ws[blockDim.x / 32] = acc;
+            }
+            __syncthreads();
+            if (ok) {
+                const int slot = base + cnt + ws[warp] + __popc(m & ((1u << lane) - 1u));
+                const uint32_t bk = bucket_of(h[i - 2], h[i - 1], a.log2_buckets);
+                keys[slot] = ((unsigned long long)bk << 32) | (uint32_t)((size_t)b * a.stride + i);
+            }
+            cnt += ws[blockDim.x / 32];
+            __syncthreads();
+        }
+        if (threadIdx.x == 0) s_total = base + cnt;
+        __syncthreads();
+    }
+    const int total = s_total;
+    int n2 = 1;
+    while (n2 < total) n2 <<= 1;
+    for (int i = total + threadIdx.x; i < n2; i += blockDim.x) keys[i] = ~0ull;  // padding sorts last
+    __syncthreads();
+    // bitonic sort, ascending
+    for (int k = 2; k <= n2; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n2; i += blockDim.x) {
+                const int l = i ^ j;
+                if (l > i) {
+                    const unsigned long long x = keys[i], y = keys[l];
+                    const bool up = (i & k) == 0;
+                    if ((x > y) == up) { keys[i] = y; keys[l] = x; }
+                }
+            }
+            __syncthreads();
+        }
+    // the first thread of each bucket's run applies the run in order
+    for (int i = threadIdx.x; i < total; i += blockDim.x) {
+        const uint32_t bk = (uint32_t)(keys[i] >> 32);
+        if (i > 0 && (uint32_t)(keys[i - 1] >> 32) == bk) continue;
+        int32_t *slots = a.table + (size_t)bk * a.slots * 2;
+        for (int r = i; r < total && (uint32_t)(keys[r] >> 32) == bk; ++r) {
+            const int32_t z = a.history[(uint32_t)keys[r]];
+            int hit = -1, empty = -1, low = 0;
+            for (int s = 0; s < a.slots; ++s) {
+                const int32_t t = slots[2 * s], c = slots[2 * s + 1];
+                if (c > 0 && t == z && hit < 0) hit = s;
+                if (c <= 0 && empty < 0) empty = s;
+                if (c < slots[2 * low + 1]) low = s;
+            }
+            if (hit >= 0) {
+                if (slots[2 * hit + 1] < INT32_MAX) slots[2 * hit + 1] += 1;
+            } else {
+                const int s = empty >= 0 ? empty : low;
+                slots[2 * s] = z;
+                slots[2 * s + 1] = 1;
+            }
+        }
+    }
+    if (threadIdx.x == 0) { a.status[0] = A11S_OK; a.status[1] = total; }
+}
+
+cudaError_t launch_ngram_update(const NgramUpdateArgs &a, cudaStream_t s) {
+    const size_t smem = (size_t)a.cap * sizeof(unsigned long long);
+    cudaError_t e = cudaFuncSetAttribute(ngram_update_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    ngram_update_kernel<<<1, kUpdThreads, smem, s>>>(a);
+    return cudaGetLastError();
+}
+
 }  // namespace a11s

@@ -11,6 +11,7 @@
  *   a11s_kv_compact       move the accepted path's KV, shrink page tables (K4)
  *   a11s_kv_reserve / a11s_kv_release / a11s_kv_free_sequences
  *                         the page allocator of the paged KV cache    (K5)
+ *   a11s_ngram_update     the n-gram table learns committed tokens    (K6)
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are caller-owned DEVICE pointers, row-major and
@@ -315,6 +316,33 @@ int a11s_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
 /* Bucket index the expansion uses for the pair (a, b); host-side helper so
  * table builders agree with the device. */
 uint32_t a11s_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets);
+
+/* ------------------------------------------------------------------------ K6
+ * The n-gram table learns committed tokens: the draft loop's other half. The
+ * reference's trigram draft (engine/speculative.py:13-24) has no learned
+ * table; its README (N-gram spec tables) names the idea, so the rule is
+ * defined here and restated by the oracle.
+ *
+ * Every history row b (history[b][0 .. history_len[b]), history_stride
+ * entries per row) adds its trigrams (h[i-2], h[i-1], h[i]), 2 <= i < len,
+ * that hold no negative token. After an acceptance step a row is
+ * (last_tokens[b][0], last_tokens[b][1], accepted_tokens[b][0 .. alen), bonus[b]).
+ * Trigram (x, y, z) updates the bucket of the pair (x, y), as a11s_ngram_bucket gives it: the slot holding
+ * z with a count > 0 gains 1 (saturating at INT32_MAX); else the lowest slot
+ * with count <= 0 becomes (z, 1); else the slot with the smallest count (the
+ * lowest index among equals) is replaced by (z, 1). Updates of one bucket
+ * apply in (row, position) order, so the result equals that serial loop.
+ * At most A11S_NGRAM_MAX_UPDATES trigrams per call: batch * (history_stride - 2)
+ * beyond it gives A11S_EUNSUPPORTED (split the batch). `status` (device
+ * int32[2]) receives A11S_OK and the number of trigrams applied, or
+ * A11S_EBOUNDS and the first row whose length is outside [0, stride] (then
+ * nothing changes). One block of 1024 threads; calls on one table must not
+ * overlap on the GPU.
+ */
+#define A11S_NGRAM_MAX_UPDATES 8192
+int a11s_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const int32_t *history,
+                      int32_t history_stride, const int32_t *history_len, int32_t batch, int32_t *status,
+                      void *stream);
 
 #ifdef __cplusplus
 }

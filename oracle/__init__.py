@@ -9,8 +9,8 @@ package and ``liba11spec.so``) never does.
   path in plain C: acceptance (rule of the reference's
   src/engine/speculative_verifier.cpp:102-132), the chunked fixed-point
   softmax, tree attention (engine/pipeline.py:386-402), compaction, the
-  paged-KV page allocator (src/cuda/paged_kv_cache.cu:85-149) and n-gram
-  expansion.
+  paged-KV page allocator (src/cuda/paged_kv_cache.cu:85-149), n-gram
+  expansion and the n-gram table update.
 * ``_ref/libref_verifier.so`` (``make ref``, only where the reference tree is
   mounted) is the reference's own ``SpeculativeTreeVerifier`` behind the
   ``ref_harness.cpp`` shim; absent on machines without the reference.
@@ -82,6 +82,7 @@ def lib():
         L.or_kv_release.argtypes = [_i32p, _i32p, C.c_int32, _i32p, C.c_int32, _i32p, C.c_int32, _i32p]
         L.or_kv_free_sequences.argtypes = [_i32p, _i32p, C.c_int32, _i32p, C.c_int32, _i32p, _i32p,
                                            C.c_int32, _i32p]
+        L.or_ngram_update.argtypes = [_i32p, C.c_int32, C.c_int32, _i32p, C.c_int32, _i32p, C.c_int32, _i32p]
         L.or_ngram_bucket.restype = C.c_uint32
         L.or_ngram_bucket.argtypes = [C.c_int32, C.c_int32, C.c_int32]
         L.or_ngram_expand.argtypes = [_i32p, C.c_int32, C.c_int32, _i32p, C.c_int32, C.c_int32,
@@ -250,6 +251,17 @@ def kv_free_sequences(stack, top, num_pages, page_table, seq_lens, mask):
 # ----------------------------------------------------------------------------- n-gram
 def ngram_bucket(a: int, b: int, log2_buckets: int) -> int:
     return int(lib().or_ngram_bucket(a, b, log2_buckets))
+
+
+def ngram_update(table, log2_buckets, history, lens):
+    """Serial restatement of a11s_ngram_update on a copy of the table."""
+    t = np.ascontiguousarray(table, dtype=np.int32).copy()
+    h = np.ascontiguousarray(history, dtype=np.int32)
+    det = np.zeros(1, np.int32)
+    rc = lib().or_ngram_update(t, log2_buckets, t.shape[1], h.reshape(-1) if h.size else np.zeros(1, np.int32),
+                               h.shape[1] if h.ndim == 2 else 0, np.ascontiguousarray(lens, dtype=np.int32),
+                               h.shape[0] if h.ndim == 2 else 0, det)
+    return dict(table=t, status=rc, detail=int(det[0]))
 
 
 def ngram_expand(table, log2_buckets, last_tokens, width_root, width_inner, max_depth, max_nodes):

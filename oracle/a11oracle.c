@@ -765,3 +765,42 @@ int or_kv_free_sequences(int32_t *stack, int32_t *top, int32_t num_pages, int32_
                          int32_t *seq_lens, const int32_t *free_mask, int32_t batch, int32_t *detail) {
     return or_kv_push(stack, top, num_pages, page_table, max_pages, seq_lens, free_mask, NULL, 0, batch, 1, detail);
 }
+
+/* ------------------------------------------------------------------------
+ * n-gram table update (a11s_ngram_update), serial: rows in order, positions
+ * in order. Trigram (x, y, z) with no negative token updates bucket(x, y):
+ * the slot holding z with count > 0 gains 1 (saturating); else the lowest
+ * slot with count <= 0 becomes (z, 1); else the slot with the smallest count
+ * (lowest index among equals) becomes (z, 1). Returns ST_EBOUNDS and the
+ * first bad row in *detail (nothing changed) or ST_OK and the count applied.
+ * ------------------------------------------------------------------------ */
+int or_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const int32_t *history,
+                    int32_t stride, const int32_t *lens, int32_t batch, int32_t *detail) {
+    for (int32_t b = 0; b < batch; ++b)
+        if (lens[b] < 0 || lens[b] > stride) { *detail = b; return ST_EBOUNDS; }
+    int32_t applied = 0;
+    for (int32_t b = 0; b < batch; ++b) {
+        const int32_t *h = history + (size_t)b * stride;
+        for (int32_t i = 2; i < lens[b]; ++i) {
+            const int32_t x = h[i - 2], y = h[i - 1], z = h[i];
+            if (x < 0 || y < 0 || z < 0) continue;
+            int32_t *sl = table + (size_t)or_ngram_bucket(x, y, log2_buckets) * slots * 2;
+            int hit = -1, empty = -1, low = 0;
+            for (int s = 0; s < slots; ++s) {
+                if (sl[2 * s + 1] > 0 && sl[2 * s] == z && hit < 0) hit = s;
+                if (sl[2 * s + 1] <= 0 && empty < 0) empty = s;
+                if (sl[2 * s + 1] < sl[2 * low + 1]) low = s;
+            }
+            if (hit >= 0) {
+                if (sl[2 * hit + 1] < 2147483647) sl[2 * hit + 1] += 1;
+            } else {
+                const int s = empty >= 0 ? empty : low;
+                sl[2 * s] = z;
+                sl[2 * s + 1] = 1;
+            }
+            ++applied;
+        }
+    }
+    *detail = applied;
+    return ST_OK;
+}

@@ -67,6 +67,9 @@ int or_kv_free_sequences(int32_t *stack, int32_t *top, int32_t num_pages, int32_
                          int32_t *seq_lens, const int32_t *free_mask, int32_t batch, int32_t *detail);
 
 uint32_t or_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets);
+/* Learning committed trigrams into the table (a11s_ngram_update), serial. */
+int or_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const int32_t *history,
+                    int32_t stride, const int32_t *lens, int32_t batch, int32_t *detail);
 int or_ngram_expand(const int32_t *table, int32_t log2_buckets, int32_t slots,
                     const int32_t *last_tokens, int32_t batch, int32_t width_root,
                     int32_t width_inner, int32_t max_depth, int32_t max_nodes, int32_t *tokens,
