@@ -171,9 +171,26 @@ def case_pages(a) -> dict:
             "pages_per_step": B * span, "status": [int(x) for x in pool.status.tolist()]}
 
 
+def case_ngram_update(a) -> dict:
+    """n-gram learning after one step: the committed tokens of `batch`
+    sequences (5 accepted + bonus each) into the C5 table (2^20 buckets)."""
+    dev = "cuda"
+    table = torch.from_numpy(W.make_ngram_table(log2_buckets=20, vocab=VOCAB, seed=1)).to(dev)
+    g = torch.Generator(device=dev).manual_seed(7)
+    B, N = a.batch, a.nodes
+    last = torch.randint(0, VOCAB, (B, 2), device=dev, dtype=torch.int32, generator=g)
+    acc = torch.randint(0, VOCAB, (B, N), device=dev, dtype=torch.int32, generator=g)
+    alen = torch.full((B,), 5, dtype=torch.int32, device=dev)
+    bonus = torch.randint(0, VOCAB, (B,), device=dev, dtype=torch.int32, generator=g)
+    hist, lens = a11spec.history_from_accept(last, acc, alen, bonus)
+    status = torch.zeros(2, dtype=torch.int32, device=dev)
+    us = _time(lambda: a11spec.ngram_update(table, hist, lens, 20, status=status), a.warmup, a.iters)
+    return {"case": "ngram_update", "batch": B, "us": us, "trigrams": int(status[1])}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram", "pages"])
+    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram", "pages", "ngram_update"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--nodes", type=int, default=64)
@@ -183,7 +200,7 @@ def main(argv=None) -> None:
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
     fn = {"attention": case_attention, "accept": case_accept, "compact": case_compact, "ngram": case_ngram,
-          "pages": case_pages}[a.case]
+          "pages": case_pages, "ngram_update": case_ngram_update}[a.case]
     print(json.dumps(fn(a)), flush=True)
 
 

@@ -255,6 +255,21 @@ class KVPagePool:
                                         mask.data_ptr(), page_table.shape[0], self.status.data_ptr(), _stream())
         self._done(rc, check_status)
 
+    def adopt(self, page_table: torch.Tensor) -> None:
+        """Set-up for tables built elsewhere: the free stack becomes every
+        pool page that no table entry holds, in ascending order (so, like the
+        reference's initial stack, the highest free id is taken first).
+        Synchronises; not for the decode loop."""
+        used = torch.zeros(self.num_pages, dtype=torch.bool, device=page_table.device)
+        ids = page_table[page_table >= 0].long()
+        if ids.numel() and (int(ids.min()) < 0 or int(ids.max()) >= self.num_pages):
+            raise A11Error(_lib.EBOUNDS, "page table holds ids outside the pool")
+        used[ids] = True
+        free = torch.nonzero(~used).flatten().to(torch.int32)
+        self.free_stack[: free.numel()] = free
+        self.free_top.fill_(free.numel())
+        torch.cuda.synchronize(page_table.device)
+
     def free_pages(self) -> torch.Tensor:
         """The stack's live entries, bottom first (a synchronising copy)."""
         return self.free_stack[: int(self.free_top.item())].clone()
@@ -262,18 +277,26 @@ class KVPagePool:
 
 # --------------------------------------------------------------------------- K6
 def history_from_accept(last_tokens: torch.Tensor, accepted_tokens: torch.Tensor, accept_len: torch.Tensor,
-                        bonus: torch.Tensor):
+                        bonus: torch.Tensor, out=None):
     """History rows of one acceptance step for ngram_update: (last_tokens[b][0],
     last_tokens[b][1], accepted_tokens[b][0 .. accept_len[b]), bonus[b]) and
-    their lengths, built with device ops (no host synchronisation)."""
+    their lengths, built with device ops (no host synchronisation). `out`:
+    preallocated (history int32 [B, N + 3], lens int32 [B]) to fill."""
     B, N = accepted_tokens.shape
-    hist = torch.full((B, N + 3), -1, dtype=torch.int32, device=accepted_tokens.device)
+    if out is None:
+        hist = torch.empty((B, N + 3), dtype=torch.int32, device=accepted_tokens.device)
+        lens_out = None
+    else:
+        hist, lens_out = out
+    hist.fill_(-1)
     hist[:, :2] = last_tokens
     hist[:, 2:2 + N] = accepted_tokens
     alen = accept_len.long().clamp(0, N)
     hist.scatter_(1, (2 + alen).unsqueeze(1), bonus.to(torch.int32).unsqueeze(1))
-    lens = (alen + 3).to(torch.int32)
-    return hist, lens
+    if lens_out is None:
+        return hist, (alen + 3).to(torch.int32)
+    torch.add(accept_len.clamp(0, N), 3, out=lens_out)
+    return hist, lens_out
 
 
 def ngram_update(table: torch.Tensor, history: torch.Tensor, lens: torch.Tensor, log2_buckets: int,

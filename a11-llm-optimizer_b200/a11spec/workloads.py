@@ -208,10 +208,13 @@ def make_ngram_table(log2_buckets: int = 20, slots: int = 8, vocab: int = VOCAB,
 def make_c5(seed: int = 5, batch: int = 32, ctx: int = 32768, max_nodes: int = 64,
             num_q_heads: int = 32, num_kv_heads: int = 4, head_dim: int = 128,
             hidden: int = 2048, vocab: int = VOCAB, log2_buckets: int = 20,
-            device: str = "cuda", temperature: float = 0.7) -> Dict:
+            device: str = "cuda", temperature: float = 0.7, spare_pages: int = 0) -> Dict:
+    """spare_pages: extra logical table entries per sequence and as many extra
+    physical pages per sequence in the pool (room for a growing context)."""
     table = torch.from_numpy(make_ngram_table(log2_buckets, 8, vocab, 1.2, seed)).to(device)
-    pool_pages = batch * ((ctx + max_nodes + 15) // 16)
-    kv = paged_kv(batch, ctx, max_nodes, num_kv_heads, head_dim, pool_pages, seed, device)
+    pool_pages = batch * ((ctx + max_nodes + 15) // 16 + spare_pages)
+    kv = paged_kv(batch, ctx, max_nodes, num_kv_heads, head_dim, pool_pages, seed, device,
+                  spare_pages=spare_pages)
     g = torch.Generator(device=device).manual_seed(seed + 3)
     q = torch.randn(batch, max_nodes, num_q_heads, head_dim, generator=g, device=device).to(torch.bfloat16)
     h = torch.randn(batch * max_nodes, hidden, generator=g, device=device).to(torch.bfloat16)

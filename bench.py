@@ -36,8 +36,8 @@ METRIC = "accepted tokens/s"
 UNIT = "tokens/s"
 B_PER_GPU, CTX, MAX_NODES, HQ, HKV, D, HIDDEN, VOCAB, TEMP = 32, 32768, 64, 32, 4, 128, 2048, 151936, 0.7
 WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH = 4, 2, 5
-# liba11spec kernels per step: n-gram expand 1, tree attention 1, accept 1, compaction 2
-LAUNCHES_PER_STEP = 5
+SPARE_PAGES = 32  # per sequence: room for the context to grow by the committed tokens
+LOG2_BUCKETS = 20
 
 
 def peaks():
@@ -143,16 +143,20 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(dev)
     B = B_PER_GPU
     st = W.make_c5(seed=5 + 1000 * rank, batch=B, ctx=CTX, max_nodes=MAX_NODES, num_q_heads=HQ,
-                   num_kv_heads=HKV, head_dim=D, hidden=HIDDEN, vocab=VOCAB, device=str(dev),
-                   temperature=TEMP)
+                   num_kv_heads=HKV, head_dim=D, hidden=HIDDEN, vocab=VOCAB, log2_buckets=LOG2_BUCKETS,
+                   device=str(dev), temperature=TEMP, spare_pages=SPARE_PAGES)
     table, q, hidden, w = st["table"], st["q"], st["hidden"], st["w"]
     k_pool, v_pool = st["k_pool"], st["v_pool"]
-    page_table0 = st["page_table"].clone()
     page_table, ctx_lens = st["page_table"], st["ctx_lens"]
+    # the device page allocator owns every page no context holds; each step
+    # reserves the drafted tree's slots and takes back what compaction detaches
+    page_table[:, (CTX + 15) // 16:] = -1
+    pages = a11spec.ops.KVPagePool(k_pool.shape[0], dev)
+    pages.adopt(page_table)
     last = st["last_tokens"]
     stats = torch.zeros(a11spec.STATS_LEN, dtype=torch.int64, device=dev)
     gen = torch.Generator(device=dev).manual_seed(77 + rank)
-    max_kv = CTX + MAX_NODES
+    max_kv = CTX + MAX_NODES + SPARE_PAGES * 16  # the context grows by the committed tokens
     # persistent buffers and workspaces: the step allocates nothing
     tree = (torch.empty(B, MAX_NODES, dtype=torch.int32, device=dev),
             torch.empty(B, MAX_NODES, dtype=torch.int32, device=dev),
@@ -160,16 +164,22 @@ def run_ours(args, rank, world, local_rank):
             torch.empty(B, dtype=torch.int32, device=dev))
     attn_out = torch.empty_like(q)
     attn_ws = a11spec.ops.workspace(a11spec.ops.tree_attention_workspace_bytes(B, MAX_NODES, HQ, HKV, D, max_kv), dev)
+    # liba11spec kernels per step: n-gram expand, page reserve, tree attention (+ split combine),
+    # accept, compaction (2), page release
+    launches_per_step = 7 + (1 if attn_ws.numel() > 256 else 0)
     logits = torch.empty(B * MAX_NODES, VOCAB, dtype=torch.bfloat16, device=dev)
     uni = torch.empty(B, MAX_NODES, dtype=torch.float32, device=dev)
     acc = a11spec.ops.alloc_accept(a11spec.STOCH_ONEHOT, B, MAX_NODES, VOCAB, dev)
     freed = torch.full_like(page_table, -1)
     n_freed = torch.zeros(B, dtype=torch.int32, device=dev)
     kv_ws = a11spec.ops.workspace(256, dev)
+    grown = torch.empty(B, dtype=torch.int32, device=dev)
     ev_attn = []
 
     def step(timed_events=None):
         tk, pa, de, nn = a11spec.ngram_expand(table, last, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES, out=tree)
+        grown.copy_(ctx_lens)
+        pages.reserve(page_table, grown, nn)  # pages for the tree slots ctx_lens + i
         if timed_events is not None:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
@@ -185,13 +195,12 @@ def run_ours(args, rank, world, local_rank):
                        temperature=TEMP, uniforms=uni, stats=stats, out=acc)
         a11spec.kv_compact(k_pool, v_pool, page_table, ctx_lens, acc.accept_len, acc.accepted_nodes,
                            nn, freed_pages=freed, n_freed=n_freed, ws=kv_ws)
-        # next root pair: (last accepted token or old root, bonus); stationary context
+        pages.release(freed, n_freed)
+        # next root pair: (last accepted token or old root, bonus)
         idx = (acc.accept_len.long() - 1).clamp_min(0).unsqueeze(1)
         prev = torch.where(acc.accept_len > 0, acc.accepted_tokens.gather(1, idx).squeeze(1), tk[:, 0])
         last[:, 0].copy_(prev)
         last[:, 1].copy_(acc.bonus.clamp_min(0))
-        page_table.copy_(page_table0)
-        ctx_lens.fill_(CTX)
         if world > 1:
             torch.distributed.all_reduce(stats.clone(), op=torch.distributed.ReduceOp.SUM)
 
@@ -272,7 +281,8 @@ def run_ours(args, rank, world, local_rank):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; no dataset exists for this path)",
-        "config": {"workload": "C5 end-to-end draft->verify->accept->compact, 32 seqs/GPU",
+        "config": {"workload": "C5 end-to-end draft->reserve pages->verify->accept->compact->release pages, "
+                               "32 seqs/GPU, context growing from 32768 by the committed tokens",
                    "seqs_per_gpu": B, "global_seqs": B * world, "ctx": CTX, "max_nodes": MAX_NODES,
                    "gqa": f"{HQ}/{HKV}", "head_dim": D, "vocab": VOCAB, "temperature": TEMP,
                    "parallelism": f"request-batch dp{world}",
@@ -285,7 +295,7 @@ def run_ours(args, rank, world, local_rank):
                      "flops_per_launch": attn_flops},
         "e2e": {"value": e2e_emitted / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo},
-        "gpu_launches": args.steps * LAUNCHES_PER_STEP,
+        "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }
     if world == 1 and not args.no_cpu_baseline:
