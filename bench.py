@@ -418,6 +418,12 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
+    # The JSON line is the only thing on stdout: file descriptor 1 points at
+    # stderr for the run (libraries such as NCCL print banners there) and the
+    # line goes to a saved copy of the real stdout.
+    sys.stdout.flush()
+    result_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -427,7 +433,7 @@ def main():
                                              device_id=torch.device("cuda", local_rank))
     line = run_reference(args, rank, world) if args.impl == "reference" else run_ours(args, rank, world, local_rank)
     if line is not None:
-        print(json.dumps(line), flush=True)
+        print(json.dumps(line), file=result_out, flush=True)
     if world > 1 and args.impl == "ours":
         torch.distributed.destroy_process_group()
 
