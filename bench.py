@@ -176,31 +176,36 @@ def run_ours(args, rank, world, local_rank):
     grown = torch.empty(B, dtype=torch.int32, device=dev)
     ev_attn = []
 
-    def step(timed_events=None):
-        tk, pa, de, nn = a11spec.ngram_expand(table, last, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES, out=tree)
+    def step(timed_events=None, inputs=None):
+        # inputs: (hidden, q, last, uniforms) of this step; default the resident
+        # set with uniforms drawn on the device
+        hid, qq, lst, un = (hidden, q, last, None) if inputs is None else inputs
+        tk, pa, de, nn = a11spec.ngram_expand(table, lst, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES, out=tree)
         grown.copy_(ctx_lens)
         pages.reserve(page_table, grown, nn)  # pages for the tree slots ctx_lens + i
         if timed_events is not None:
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
-        a11spec.tree_attention(q, k_pool, v_pool, page_table, ctx_lens, pa, nn, max_kv_len=max_kv,
+        a11spec.tree_attention(qq, k_pool, v_pool, page_table, ctx_lens, pa, nn, max_kv_len=max_kv,
                                out=attn_out, ws=attn_ws)
         if timed_events is not None:
             e1.record()
             timed_events.append((e0, e1))
-        torch.matmul(hidden, w, out=logits)
-        uni.uniform_(generator=gen)
+        torch.matmul(hid, w, out=logits)
+        if un is None:
+            uni.uniform_(generator=gen)
+            un = uni
         a11spec.accept(a11spec.STOCH_ONEHOT, logits.view(B, MAX_NODES, VOCAB), tk, pa, nn,
-                       temperature=TEMP, uniforms=uni, stats=stats, out=acc)
+                       temperature=TEMP, uniforms=un, stats=stats, out=acc)
         a11spec.kv_compact(k_pool, v_pool, page_table, ctx_lens, acc.accept_len, acc.accepted_nodes,
                            nn, freed_pages=freed, n_freed=n_freed, ws=kv_ws)
         pages.release(freed, n_freed)
         # next root pair: (last accepted token or old root, bonus)
         idx = (acc.accept_len.long() - 1).clamp_min(0).unsqueeze(1)
         prev = torch.where(acc.accept_len > 0, acc.accepted_tokens.gather(1, idx).squeeze(1), tk[:, 0])
-        last[:, 0].copy_(prev)
-        last[:, 1].copy_(acc.bonus.clamp_min(0))
+        lst[:, 0].copy_(prev)
+        lst[:, 1].copy_(acc.bonus.clamp_min(0))
         if world > 1:
             torch.distributed.all_reduce(stats.clone(), op=torch.distributed.ReduceOp.SUM)
 
@@ -238,25 +243,45 @@ def run_ours(args, rank, world, local_rank):
     bi = sum(t.numel() * t.element_size() for t in (h_hidden, h_q, h_uni, h_last))
     bo = sum(t.numel() * t.element_size() for t in (h_out_tok, h_out_len, h_out_bonus))
 
-    def e2e_step():
-        hidden.copy_(h_hidden, non_blocking=True)
-        q.copy_(h_q, non_blocking=True)
-        last.copy_(h_last, non_blocking=True)
-        step()
-        h_out_tok.copy_(acc.accepted_tokens, non_blocking=True)
-        h_out_len.copy_(acc.accept_len, non_blocking=True)
-        h_out_bonus.copy_(acc.bonus, non_blocking=True)
+    # Two input sets: step k+1's H2D runs on a copy stream while step k
+    # computes (a serving loop's double buffering); step k waits for its own
+    # copy, and a set is refilled only after the step that read it.
+    copy_stream = torch.cuda.Stream(device=dev)
+    ins = [(hidden, q, last, torch.empty_like(uni)),
+           (hidden.clone(), q.clone(), last.clone(), torch.empty_like(uni))]
+    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    free = [torch.cuda.Event(), torch.cuda.Event()]
 
-    for _ in range(max(1, args.warmup // 2)):
-        e2e_step()
+    def h2d(k):
+        dst = ins[k % 2]
+        with torch.cuda.stream(copy_stream):
+            if k >= 2:
+                copy_stream.wait_event(free[k % 2])
+            for d_, h_ in zip(dst, (h_hidden, h_q, h_last, h_uni)):
+                d_.copy_(h_, non_blocking=True)
+            ready[k % 2].record(copy_stream)
+
+    def e2e_run(n):
+        copy_stream.wait_stream(torch.cuda.current_stream())  # copies start after the timing event
+        h2d(0)
+        for k in range(n):
+            if k + 1 < n:
+                h2d(k + 1)
+            torch.cuda.current_stream().wait_event(ready[k % 2])
+            step(inputs=ins[k % 2])
+            free[k % 2].record()
+            h_out_tok.copy_(acc.accepted_tokens, non_blocking=True)
+            h_out_len.copy_(acc.accept_len, non_blocking=True)
+            h_out_bonus.copy_(acc.bonus, non_blocking=True)
+
+    e2e_run(max(1, args.warmup // 2))
     barrier()
     s1 = stats.clone()
     x0, x1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with ClockSampler(gpu_id(dev)) as clk_e2e:  # the clock record covers both timed regions
         barrier()
         x0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         x1.record()
         barrier()
     clk.lines.extend(clk_e2e.lines)
