@@ -6,6 +6,7 @@ ABI of include/a11spec.h); this package is the PyTorch-facing host layer:
 * ``ops``        torch wrappers of the kernels (draft, attention, accept, compact,
                  page allocator ``KVPagePool``, n-gram learning ``ngram_update``)
 * ``ngram_table`` the n-gram table's file format
+* ``generate``   ``speculative_stream``: the speculative decode loop around a target model
 * ``decoder``    ``SpeculativeDecoder`` with the method names of the reference's
                  engine/speculative.py, plus batched tree APIs
 * ``workloads``  seeded synthetic inputs of the five benchmark configurations

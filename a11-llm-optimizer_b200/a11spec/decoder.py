@@ -45,6 +45,7 @@ class SpeculativeDecoder:
         if table is None:
             table = torch.zeros((1 << log2_buckets, 8, 2), dtype=torch.int32)
         self.table = table.to(self.device, torch.int32).contiguous()
+        self.log2_buckets = log2_buckets
         self.width_root, self.width_inner = width_root, width_inner
         self.max_depth, self.max_nodes = max_depth, max_nodes
         self.temperature = temperature
