@@ -514,22 +514,36 @@ __global__ void tree_attn_combine(const TcParams p) {
     const int node = (int)((row / p.Hq) % p.N);
     int n_live = p.n_nodes ? p.n_nodes[b] : p.N;
     if (n_live < 1 || n_live > p.N) n_live = 0;
+    // online merge, 4 splits per group with all their loads in flight together
     float4 acc = make_float4(0, 0, 0, 0);
     float M = -INFINITY, wsum = 0.0f;
     if (node < n_live) {
-        for (int s = 0; s < p.splits; ++s) {
-            const size_t prow = (size_t)s * rows + row;
-            const float ms = p.part_ml[prow * 2], ls = p.part_ml[prow * 2 + 1];
-            if (ls > 0.0f) M = fmaxf(M, ms);
-        }
-        for (int s = 0; s < p.splits; ++s) {
-            const size_t prow = (size_t)s * rows + row;
-            const float ms = p.part_ml[prow * 2], ls = p.part_ml[prow * 2 + 1];
-            if (!(ls > 0.0f)) continue;
-            const float w = ls * exp2f(ms - M);
-            const float4 o = reinterpret_cast<const float4 *>(p.part_o + prow * 128)[lane];
-            acc.x += w * o.x; acc.y += w * o.y; acc.z += w * o.z; acc.w += w * o.w;
-            wsum += w;
+        for (int s0 = 0; s0 < p.splits; s0 += 4) {
+            float ms[4], ls[4];
+            float4 o[4];
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                const size_t prow = (size_t)min(s0 + g, p.splits - 1) * rows + row;
+                ms[g] = p.part_ml[prow * 2];
+                ls[g] = s0 + g < p.splits ? p.part_ml[prow * 2 + 1] : 0.0f;
+                o[g] = reinterpret_cast<const float4 *>(p.part_o + prow * 128)[lane];
+            }
+            float Mg = M;
+#pragma unroll
+            for (int g = 0; g < 4; ++g)
+                if (ls[g] > 0.0f) Mg = fmaxf(Mg, ms[g]);
+            if (Mg == -INFINITY) continue;
+            const float a = M == -INFINITY ? 0.0f : exp2f(M - Mg);
+            acc.x *= a; acc.y *= a; acc.z *= a; acc.w *= a;
+            wsum *= a;
+#pragma unroll
+            for (int g = 0; g < 4; ++g) {
+                if (!(ls[g] > 0.0f)) continue;
+                const float w = ls[g] * exp2f(ms[g] - Mg);
+                acc.x += w * o[g].x; acc.y += w * o[g].y; acc.z += w * o[g].z; acc.w += w * o[g].w;
+                wsum += w;
+            }
+            M = Mg;
         }
     }
     const float inv = wsum > 0.0f ? 1.0f / wsum : 0.0f;
