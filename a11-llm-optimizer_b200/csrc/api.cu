@@ -64,6 +64,13 @@ AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32
     return L;
 }
 
+// An empty batch launches nothing, but the caller may still read the
+// workspace status word afterwards: clear it on the stream.
+int empty_batch_status(void *workspace, size_t workspace_bytes, void *stream, const char *who) {
+    if (!workspace || workspace_bytes < sizeof(a11s::StatusWord)) return A11S_OK;
+    const cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(a11s::StatusWord), reinterpret_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? A11S_OK : cuda_fail(e, who);
+}
 }  // namespace
 
 namespace a11s {
@@ -116,7 +123,7 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
         return fail(A11S_EINVAL,
                     "a11s_accept: row_stride %lld and vocab %d must be multiples of %d, stride >= vocab",
                     (long long)row_stride, vocab, vec);
-    if (batch == 0) return A11S_OK;
+    if (batch == 0) return empty_batch_status(workspace, workspace_bytes, stream, "a11s_accept: clearing status");
     if (!target_logits || !tokens || !parents || !accept_len || !accepted_nodes ||
         !accepted_tokens || !bonus || !workspace)
         return fail(A11S_EINVAL, "a11s_accept: null required pointer");
@@ -187,7 +194,7 @@ int a11s_verify_chain(const float *draft_probs, const float *target_probs, const
                       int32_t batch, int32_t n, int32_t *accepted_len, int32_t *last_idx,
                       void *workspace, size_t workspace_bytes, void *stream) {
     if (batch < 0 || n < 0) return fail(A11S_EINVAL, "a11s_verify_chain: negative size");
-    if (batch == 0) return A11S_OK;
+    if (batch == 0) return empty_batch_status(workspace, workspace_bytes, stream, "a11s_verify_chain: clearing status");
     if (!accepted_len || !last_idx || !workspace || (n > 0 && (!draft_probs || !target_probs || !uniforms)))
         return fail(A11S_EINVAL, "a11s_verify_chain: null required pointer");
     if (workspace_bytes < sizeof(a11s::StatusWord))
@@ -219,7 +226,7 @@ int a11s_kv_compact(void *k_pool, void *v_pool, int32_t num_layers, int64_t laye
     const int64_t slab = (int64_t)num_pages * A11S_PAGE_TOKENS * row_elems;
     if (num_layers > 1 && layer_stride < slab)
         return fail(A11S_EINVAL, "a11s_kv_compact: layer_stride smaller than one layer");
-    if (batch == 0) return A11S_OK;
+    if (batch == 0) return empty_batch_status(workspace, workspace_bytes, stream, "a11s_kv_compact: clearing status");
     if (!k_pool || !v_pool || !page_table || !seq_lens || !accept_len || !accepted_nodes)
         return fail(A11S_EINVAL, "a11s_kv_compact: null required pointer");
     if (!aligned16(k_pool) || !aligned16(v_pool))
@@ -392,7 +399,7 @@ int a11s_tree_attention(const void *q, const void *k_pool, const void *v_pool, i
     if ((int64_t)max_pages_per_seq * A11S_PAGE_TOKENS < max_kv_len)
         return fail(A11S_EINVAL, "a11s_tree_attention: page table shorter than max_kv_len");
     if (!(scale > 0.0f) || !std::isfinite(scale)) return fail(A11S_EINVAL, "a11s_tree_attention: bad scale");
-    if (batch == 0) return A11S_OK;
+    if (batch == 0) return empty_batch_status(workspace, workspace_bytes, stream, "a11s_tree_attention: clearing status");
     if (!q || !k_pool || !v_pool || !page_table || !ctx_lens || !parents || !out || !workspace)
         return fail(A11S_EINVAL, "a11s_tree_attention: null required pointer");
     if (!aligned16(q) || !aligned16(k_pool) || !aligned16(v_pool) || !aligned16(out) || !aligned16(workspace))

@@ -203,24 +203,34 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         tc::fence_barrier_init();
     }
     if (warp == kProducerWarp) {
-        // ancestor-or-self bits of the CTA's nodes (lane = node offset)
+        // ancestor-or-self bits of the CTA's nodes (lane = node offset). The
+        // sequence's parents (N <= 64) sit in two registers per lane, read
+        // with one coalesced load; each step up the tree is two shuffles.
+        const int32_t *par = p.parents + (size_t)b * p.N;
+        const int32_t r0 = lane < p.N ? par[lane] : -1;
+        const int32_t r1 = lane + 32 < p.N ? par[lane + 32] : -1;
         const int nd = node0 + lane;
         uint64_t anc = 0;
-        if (nd < n_live) {
-            const int32_t *par = p.parents + (size_t)b * p.N;
-            int a = nd;
-            bool ok = false;
-            for (int steps = 0; steps <= 64; ++steps) {
+        int a = nd;
+        bool done = !(nd < n_live), ok = false;
+        for (int steps = 0; steps <= 64; ++steps) {
+            if (!__any_sync(0xffffffffu, !done)) break;
+            const int v0 = __shfl_sync(0xffffffffu, r0, a & 31), v1 = __shfl_sync(0xffffffffu, r1, a & 31);
+            if (!done) {
                 anc |= 1ull << a;
-                if (a == 0) { ok = true; break; }
-                const int pa = par[a];
-                if (pa < 0 || pa >= a) break;
-                a = pa;
+                if (a == 0) {
+                    ok = true;
+                    done = true;
+                } else {
+                    const int pa = a < 32 ? v0 : v1;
+                    if (pa < 0 || pa >= a) done = true;
+                    else a = pa;
+                }
             }
-            if (!ok) {
-                report(p.status, A11S_EBOUNDS, b);
-                anc = 1ull << nd;
-            }
+        }
+        if (nd < n_live && !ok) {
+            report(p.status, A11S_EBOUNDS, b);
+            anc = 1ull << nd;
         }
         bs->anc[lane] = anc;
     }

@@ -40,9 +40,16 @@ def _tree(rng, B, N, V, x, p_force=0.7):
 
 def test_empty_batches(dev):
     V, N = 4096, 8
+    ws = torch.full((256,), 255, dtype=torch.uint8, device=dev)  # a stale status word must be cleared
     r = a11spec.accept(0, torch.zeros(0, N, V, device=dev), torch.zeros(0, N, dtype=torch.int32, device=dev),
-                       torch.zeros(0, N, dtype=torch.int32, device=dev), check_status=True)
+                       torch.zeros(0, N, dtype=torch.int32, device=dev), ws=ws, check_status=True)
     assert r.accept_len.numel() == 0
+    ws.fill_(255)
+    q = torch.zeros(0, N, 16, 128, dtype=torch.bfloat16, device=dev)
+    pool = torch.zeros(4, 16, 2, 128, dtype=torch.bfloat16, device=dev)
+    a11spec.tree_attention(q, pool, pool, torch.zeros(0, 4, dtype=torch.int32, device=dev),
+                           torch.zeros(0, dtype=torch.int32, device=dev), torch.zeros(0, N, dtype=torch.int32, device=dev),
+                           ws=ws, check_status=True)
     table = torch.zeros(1 << 6, 4, 2, dtype=torch.int32, device=dev)
     tk, pa, de, nn = a11spec.ngram_expand(table, torch.zeros(0, 2, dtype=torch.int32, device=dev), 2, 1, 3, 8)
     assert tk.numel() == 0
