@@ -8,17 +8,20 @@
 // Semantics: include/a11spec.h (a11s_tree_attention).
 //
 // One CTA = one sequence b, one KV head g, 32 tree nodes x 8 query heads as
-// two Q tiles of 128 rows (the MMA M), one split of the KV range. 320 threads:
+// two Q tiles of 128 rows (the MMA M), one split of the KV range. 384 threads:
 //   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane
 //   warp 8     TMA producer: Q once, then K and V blocks of 128 keys (8 pages,
 //              one 64x16 box per page and 64-column half) into a 3-slot K
 //              ring and a 2-slot V ring shared by both tiles (a K slot frees
 //              after QK^T, long before PV); page ids fetched 4 blocks ahead
 //   warp 9     TMEM allocator + single-thread MMA issuer
+//   warps 10-11 idle (they complete the third warpgroup for the register split:
+//              softmax warps 216 registers, warps 8-11 56)
 // TMEM (512 columns): per tile one S/P buffer of 128 columns and O (128 dims).
 // Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N128 K16), the
-// softmax warps mask it (ancestor bits), exponentiate with one FFMA + ex2 per
-// score, pack P_j to bf16 with integer ops and store it over the first 64
+// softmax warps mask it (ancestor bits), exponentiate (one packed FFMA per
+// pair of scores, one ex2 each), round P_j to bf16 (nearest even) and, with
+// fp32 row sums of the unrounded values, store it over the first 64
 // columns of the same buffer, then O += P_j V_j (8 MMAs M128 N128 K16, A = P
 // read from TMEM, V an MN-major shared-memory operand). S_{j+1} of a tile is
 // issued once PV_j of that tile has completed (S and P share columns); the
@@ -52,7 +55,9 @@ constexpr int kNodesPerTile = 16;
 constexpr int kNodesPerCta = kTiles * kNodesPerTile;
 constexpr int kSoftmaxWarps = 4 * kTiles;
 constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
-constexpr int kTcThreads = 32 * (kSoftmaxWarps + 2);
+constexpr int kTcThreads = 32 * (kSoftmaxWarps + 4);  // + producer, issuer, 2 idle: whole warpgroups
+constexpr int kRegsSoftmax = 216, kRegsOther = 56;    // setmaxnreg split (multiples of 8)
+constexpr long long kRegsNeeded = 32ll * (kSoftmaxWarps * kRegsSoftmax + 4 * kRegsOther);
 constexpr uint32_t kQHalf = 16384;    // Q tile: 128 rows x 128 B per 64-dim half
 constexpr uint32_t kKVHalf = 16384;   // K or V: 128 tokens x 128 B per 64-dim half
 constexpr uint32_t kOffQ = 0;                                // tile t at 2*kQHalf*t
@@ -123,12 +128,6 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, Ba
     *reinterpret_cast<volatile int32_t *>(&bs->abort) = 1;
     report(st, A11S_ETIMEOUT, 0);
     return false;
-}
-
-// bf16 pair by rounding half up on the bit patterns (a >= 0 and finite here):
-// unbiased to within the half-way ties, two integer adds and one byte permute.
-__device__ __forceinline__ uint32_t pack_bf16x2(float a0, float a1) {
-    return __byte_perm(__float_as_uint(a0) + 0x8000u, __float_as_uint(a1) + 0x8000u, 0x7632);
 }
 
 // Three-input maximum (one instruction on sm_100).
@@ -243,136 +242,144 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     tc::tc_fence_after();
     const uint32_t tmem = bs->tmem_base;
 
-    if (warp == kProducerWarp) {
-        // ---------------- TMA producer ----------------
-        if (lane == 0) {
-            tc::prefetch_tmap(&tq);
-            tc::prefetch_tmap(&tk);
-            tc::prefetch_tmap(&tv);
-            tc::mbar_arrive_expect_tx(&bs->q_full, kTiles * 2 * kQHalf);
-            for (int t = 0; t < kTiles; ++t) {
-                const int qrow = b * p.N + node0 + t * kNodesPerTile;
-                uint8_t *sQ = sm + kOffQ + t * 2 * kQHalf;
-                tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
-                tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
-            }
-        }
-        // Page ids of 4 blocks (32 entries) per coalesced warp load, double
-        // buffered, so a block's ids were requested 4 blocks before use.
-        constexpr int kBlocksPerWindow = 32 / kPagesPerBlock;
-        const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
-        const int lp0 = blk0 * kPagesPerBlock;
-        const int lp_end = min((kv_len + A11S_PAGE_TOKENS - 1) / A11S_PAGE_TOKENS, (blk0 + nb) * kPagesPerBlock);
-        auto window = [&](int w) -> int {  // entry lp0 + 32 w + lane, or -2 past the needed range
-            const int lp = lp0 + 32 * w + lane;
-            if (lp >= lp_end) return -2;
-            return lp < p.max_pages ? __ldg(pt + lp) : -1;
-        };
-        int cur = window(0), nxt = window(1);
-        int nk = 0, nv = 0;  // K and V blocks whose loads were issued
-        for (int it = 0; it < nb && !aborted(bs); ++it) {
-            const int k = it % kBlocksPerWindow;
-            if (k == 0 && it > 0) {
-                cur = nxt;
-                nxt = window(it / kBlocksPerWindow + 1);
-            }
-            const int id = __shfl_sync(0xffffffffu, cur, (k * kPagesPerBlock + lane) & 31);
-            int page = p.num_pages;  // out of range -> zero fill
-            if (lane < kPagesPerBlock && id != -2) {
-                if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
-                else page = id;
-            }
-            // K(it): its slot was last read by QK(it - kKStages)
-            const int ks = it % kKStages, kuse = it / kKStages;
-            if (lane == 0 && kuse > 0) wait_or_abort(&bs->k_empty[ks], (kuse - 1) & 1, bs, p.status);
-            __syncwarp();
-            if (aborted(bs)) break;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->k_full[ks], kSlotBytes);
-            __syncwarp();
-            uint8_t *sK = sm + kOffK + ks * kSlotBytes;
-            if (lane < kPagesPerBlock) {
-                tc::tma_load_4d(sK + lane * 2048, &tk, &bs->k_full[ks], 0, g, 0, page);
-                tc::tma_load_4d(sK + kKVHalf + lane * 2048, &tk, &bs->k_full[ks], 64, g, 0, page);
-            }
-            ++nk;
-            // V(it): its slot was last read by PV(it - kVStages)
-            const int vs = it % kVStages, vuse = it / kVStages;
-            if (lane == 0 && vuse > 0) wait_or_abort(&bs->v_empty[vs], (vuse - 1) & 1, bs, p.status);
-            __syncwarp();
-            if (aborted(bs)) break;
-            if (lane == 0) tc::mbar_arrive_expect_tx(&bs->v_full[vs], kSlotBytes);
-            __syncwarp();
-            uint8_t *sV = sm + kOffV + vs * kSlotBytes;
-            if (lane < kPagesPerBlock) {
-                tc::tma_load_4d(sV + lane * 2048, &tv, &bs->v_full[vs], 0, g, 0, page);
-                tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->v_full[vs], 64, g, 0, page);
-            }
-            ++nv;
-        }
-        if (aborted(bs) && lane == 0) {
-            // drain copies that may still be landing in this CTA's shared memory
-            tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
-            for (int i = max(0, nk - kKStages); i < nk; ++i)
-                tc::mbar_wait(&bs->k_full[i % kKStages], (i / kKStages) & 1, kWaitBudget);
-            for (int i = max(0, nv - kVStages); i < nv; ++i)
-                tc::mbar_wait(&bs->v_full[i % kVStages], (i / kVStages) & 1, kWaitBudget);
-        }
-    } else if (warp == kMmaWarp) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
-            auto issue_s = [&](int it, int t) {  // S(it) of tile t: 8 MMAs M128 N128 K16
-                const uint32_t k_addr = tc::smem_u32(sm + kOffK + (it % kKStages) * kSlotBytes);
-                const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
-#pragma unroll
-                for (int kk = 0; kk < 8; ++kk) {
-                    const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-                    const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                    tc::mma_bf16_ss(tmem + t * 128, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
-                                    tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
+    // Register split per warpgroup (setmaxnreg acts on whole warpgroups):
+    // warps 8-11 give registers back, the softmax warps take them. The total
+    // stays within the launch's registers (checked on the host before launch).
+    static_assert(kRegsSoftmax % 8 == 0 && kRegsOther % 8 == 0, "setmaxnreg counts");
+    if (warp >= kSoftmaxWarps) {
+        asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(kRegsOther));
+        if (warp == kProducerWarp) {
+            // ---------------- TMA producer ----------------
+            if (lane == 0) {
+                tc::prefetch_tmap(&tq);
+                tc::prefetch_tmap(&tk);
+                tc::prefetch_tmap(&tv);
+                tc::mbar_arrive_expect_tx(&bs->q_full, kTiles * 2 * kQHalf);
+                for (int t = 0; t < kTiles; ++t) {
+                    const int qrow = b * p.N + node0 + t * kNodesPerTile;
+                    uint8_t *sQ = sm + kOffQ + t * 2 * kQHalf;
+                    tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
+                    tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
                 }
-                tc::mma_commit(&bs->s_full[t]);
-                if (t == kTiles - 1) tc::mma_commit(&bs->k_empty[it % kKStages]);
+            }
+            // Page ids of 4 blocks (32 entries) per coalesced warp load, double
+            // buffered, so a block's ids were requested 4 blocks before use.
+            constexpr int kBlocksPerWindow = 32 / kPagesPerBlock;
+            const int32_t *pt = p.page_table + (size_t)b * p.max_pages;
+            const int lp0 = blk0 * kPagesPerBlock;
+            const int lp_end = min((kv_len + A11S_PAGE_TOKENS - 1) / A11S_PAGE_TOKENS, (blk0 + nb) * kPagesPerBlock);
+            auto window = [&](int w) -> int {  // entry lp0 + 32 w + lane, or -2 past the needed range
+                const int lp = lp0 + 32 * w + lane;
+                if (lp >= lp_end) return -2;
+                return lp < p.max_pages ? __ldg(pt + lp) : -1;
             };
-            bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
-            ok = ok && wait_or_abort(&bs->k_full[0], 0, bs, p.status);
-            if (ok) {
-                tc::tc_fence_after();
-                for (int t = 0; t < kTiles; ++t) issue_s(0, t);
+            int cur = window(0), nxt = window(1);
+            int nk = 0, nv = 0;  // K and V blocks whose loads were issued
+            for (int it = 0; it < nb && !aborted(bs); ++it) {
+                const int k = it % kBlocksPerWindow;
+                if (k == 0 && it > 0) {
+                    cur = nxt;
+                    nxt = window(it / kBlocksPerWindow + 1);
+                }
+                const int id = __shfl_sync(0xffffffffu, cur, (k * kPagesPerBlock + lane) & 31);
+                int page = p.num_pages;  // out of range -> zero fill
+                if (lane < kPagesPerBlock && id != -2) {
+                    if (id < 0 || id >= p.num_pages) report(p.status, A11S_EBOUNDS, b);
+                    else page = id;
+                }
+                // K(it): its slot was last read by QK(it - kKStages)
+                const int ks = it % kKStages, kuse = it / kKStages;
+                if (lane == 0 && kuse > 0) wait_or_abort(&bs->k_empty[ks], (kuse - 1) & 1, bs, p.status);
+                __syncwarp();
+                if (aborted(bs)) break;
+                if (lane == 0) tc::mbar_arrive_expect_tx(&bs->k_full[ks], kSlotBytes);
+                __syncwarp();
+                uint8_t *sK = sm + kOffK + ks * kSlotBytes;
+                if (lane < kPagesPerBlock) {
+                    tc::tma_load_4d(sK + lane * 2048, &tk, &bs->k_full[ks], 0, g, 0, page);
+                    tc::tma_load_4d(sK + kKVHalf + lane * 2048, &tk, &bs->k_full[ks], 64, g, 0, page);
+                }
+                ++nk;
+                // V(it): its slot was last read by PV(it - kVStages)
+                const int vs = it % kVStages, vuse = it / kVStages;
+                if (lane == 0 && vuse > 0) wait_or_abort(&bs->v_empty[vs], (vuse - 1) & 1, bs, p.status);
+                __syncwarp();
+                if (aborted(bs)) break;
+                if (lane == 0) tc::mbar_arrive_expect_tx(&bs->v_full[vs], kSlotBytes);
+                __syncwarp();
+                uint8_t *sV = sm + kOffV + vs * kSlotBytes;
+                if (lane < kPagesPerBlock) {
+                    tc::tma_load_4d(sV + lane * 2048, &tv, &bs->v_full[vs], 0, g, 0, page);
+                    tc::tma_load_4d(sV + kKVHalf + lane * 2048, &tv, &bs->v_full[vs], 64, g, 0, page);
+                }
+                ++nv;
             }
-            // Per block and tile: PV(it) once the tile's P is in TMEM, then
-            // S(it + 1) once PV(it) has read P (S and P share the columns).
-            // The other tile's softmax runs meanwhile, so the tensor pipe
-            // alternates between the tiles.
-            for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
-                const int vs = it % kVStages;
-                const uint32_t v_addr = tc::smem_u32(sm + kOffV + vs * kSlotBytes);
-                for (int t = 0; t < kTiles && ok; ++t) {
-                    if (!wait_or_abort(&bs->p_full[t], it & 1, bs, p.status)) { ok = false; break; }
-                    if (t == 0 && !wait_or_abort(&bs->v_full[vs], (it / kVStages) & 1, bs, p.status)) { ok = false; break; }
-                    tc::tc_fence_after();
-#pragma unroll
-                    for (int kk = 0; kk < kBlockKV / 16; ++kk) {
-                        tc::mma_bf16_ts(tmem + kColO + t * 128, tmem + t * 128 + kk * 8,
-                                        tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
-                                        (it > 0 || kk > 0) ? 1u : 0u);
+            if (aborted(bs) && lane == 0) {
+                // drain copies that may still be landing in this CTA's shared memory
+                tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
+                for (int i = max(0, nk - kKStages); i < nk; ++i)
+                    tc::mbar_wait(&bs->k_full[i % kKStages], (i / kKStages) & 1, kWaitBudget);
+                for (int i = max(0, nv - kVStages); i < nv; ++i)
+                    tc::mbar_wait(&bs->v_full[i % kVStages], (i / kVStages) & 1, kWaitBudget);
+            }
+        } else if (warp == kMmaWarp) {
+            // ---------------- MMA issuer ----------------
+            if (lane == 0) {
+                auto issue_s = [&](int it, int t) {  // S(it) of tile t: 8 MMAs M128 N128 K16
+                    const uint32_t k_addr = tc::smem_u32(sm + kOffK + (it % kKStages) * kSlotBytes);
+                    const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
+    #pragma unroll
+                    for (int kk = 0; kk < 8; ++kk) {
+                        const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
+                        const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
+                        tc::mma_bf16_ss(tmem + t * 128, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
+                                        tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
                     }
-                    tc::mma_commit(&bs->p_free[t]);
-                    if (t == kTiles - 1) tc::mma_commit(&bs->v_empty[vs]);
-                    if (it + 1 < nb) {
-                        if (t == 0 && !wait_or_abort(&bs->k_full[(it + 1) % kKStages], ((it + 1) / kKStages) & 1, bs,
-                                                     p.status)) { ok = false; break; }
-                        if (!wait_or_abort(&bs->p_free[t], it & 1, bs, p.status)) { ok = false; break; }
+                    tc::mma_commit(&bs->s_full[t]);
+                    if (t == kTiles - 1) tc::mma_commit(&bs->k_empty[it % kKStages]);
+                };
+                bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
+                ok = ok && wait_or_abort(&bs->k_full[0], 0, bs, p.status);
+                if (ok) {
+                    tc::tc_fence_after();
+                    for (int t = 0; t < kTiles; ++t) issue_s(0, t);
+                }
+                // Per block and tile: PV(it) once the tile's P is in TMEM, then
+                // S(it + 1) once PV(it) has read P (S and P share the columns).
+                // The other tile's softmax runs meanwhile, so the tensor pipe
+                // alternates between the tiles.
+                for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
+                    const int vs = it % kVStages;
+                    const uint32_t v_addr = tc::smem_u32(sm + kOffV + vs * kSlotBytes);
+                    for (int t = 0; t < kTiles && ok; ++t) {
+                        if (!wait_or_abort(&bs->p_full[t], it & 1, bs, p.status)) { ok = false; break; }
+                        if (t == 0 && !wait_or_abort(&bs->v_full[vs], (it / kVStages) & 1, bs, p.status)) { ok = false; break; }
                         tc::tc_fence_after();
-                        issue_s(it + 1, t);
+    #pragma unroll
+                        for (int kk = 0; kk < kBlockKV / 16; ++kk) {
+                            tc::mma_bf16_ts(tmem + kColO + t * 128, tmem + t * 128 + kk * 8,
+                                            tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
+                                            (it > 0 || kk > 0) ? 1u : 0u);
+                        }
+                        tc::mma_commit(&bs->p_free[t]);
+                        if (t == kTiles - 1) tc::mma_commit(&bs->v_empty[vs]);
+                        if (it + 1 < nb) {
+                            if (t == 0 && !wait_or_abort(&bs->k_full[(it + 1) % kKStages], ((it + 1) / kKStages) & 1, bs,
+                                                         p.status)) { ok = false; break; }
+                            if (!wait_or_abort(&bs->p_free[t], it & 1, bs, p.status)) { ok = false; break; }
+                            tc::tc_fence_after();
+                            issue_s(it + 1, t);
+                        }
                     }
                 }
+                // wait for every issued MMA before the CTA may release TMEM
+                tc::mma_commit(&bs->drain);
+                tc::mbar_wait(&bs->drain, 0, kWaitBudget);
             }
-            // wait for every issued MMA before the CTA may release TMEM
-            tc::mma_commit(&bs->drain);
-            tc::mbar_wait(&bs->drain, 0, kWaitBudget);
+            __syncwarp();
         }
-        __syncwarp();
     } else {
+        asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
         // ---------------- softmax warps: tile = warp / 4, thread = query row ----------------
         const bool live = node < n_live;
         const uint64_t anc = bs->anc[node - node0];
@@ -423,7 +430,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
-            float ls[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // independent partial sums
+            float2 ls[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
             // P as bf16 pairs (lower key in the low half) over the first 64
             // columns of the S buffer, in four stores of 32 keys (S is in
             // registers, so overwriting its columns is safe), one wait at the end.
@@ -432,16 +439,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 uint32_t pw[16];
 #pragma unroll
                 for (int c = 0; c < 16; ++c) {
-                    const float a0 = tc::ex2(fmaf(X(32 * h + 2 * c), sl2, neg));
-                    const float a1 = tc::ex2(fmaf(X(32 * h + 2 * c + 1), sl2, neg));
-                    pw[c] = pack_bf16x2(a0, a1);
-                    ls[(2 * c) & 7] += a0;  // exact fp32 denominator; P is rounded to nearest
-                    ls[(2 * c + 1) & 7] += a1;
+                    const float2 e = tc::ffma2(make_float2(X(32 * h + 2 * c), X(32 * h + 2 * c + 1)),
+                                               make_float2(sl2, sl2), make_float2(neg, neg));
+                    const float2 a = make_float2(tc::ex2(e.x), tc::ex2(e.y));
+                    pw[c] = tc::cvt_bf16x2(a.x, a.y);
+                    ls[c & 3] = tc::fadd2(ls[c & 3], a);  // fp32 denominator of the unrounded p
                 }
                 tc::tmem_st16u_nowait(tmem + lane_base + col_s + 16 * h, pw);
             }
             tc::tmem_wait_st();
-            lsum = lsum * alpha + (((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7])));
+            lsum = lsum * alpha + (((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y)));
             // Rescale O (after the scores are dead, before PV(it) may start):
             // PV(it-1) has completed, since S(it) was computed after it.
             if (__any_sync(0xffffffffu, rescale) && it > 0) {
@@ -609,6 +616,12 @@ cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
     }
     cudaError_t ea = cudaFuncSetAttribute(tree_attn_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
     if (ea != cudaSuccess) return ea;
+    {  // setmaxnreg.inc would wait forever if the split needed more registers than the launch holds
+        cudaFuncAttributes fa{};
+        ea = cudaFuncGetAttributes(&fa, tree_attn_tc);
+        if (ea != cudaSuccess) return ea;
+        if ((long long)fa.numRegs * kTcThreads < kRegsNeeded) return cudaErrorInvalidConfiguration;
+    }
     TcParams p{};
     p.page_table = a.page_table;
     p.max_pages = a.max_pages;
