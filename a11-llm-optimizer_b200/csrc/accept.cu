@@ -3,11 +3,13 @@
 // One kernel per call; block (x, y) = (sequence, slice of its units), so the
 // first wave holds every sequence's first slice.
 // Phase 1 (every block, HBM-bound): warps stream 2048-token chunks of every
-//   live logits row with 16-byte non-allocating loads and keep the chunk
-//   maximum (NaN-propagating, so a NaN or +Inf is caught here): two
-//   instructions per logit, the single read of the vocab. A sequence's units
-//   start with its root rows; only their maxima are recorded (and, in the
-//   sampling modes, their fixed-point weight sums).
+//   live logits row with 16-byte non-allocating loads and record the chunk
+//   maximum (NaN-propagating, so a NaN or +Inf is caught here; GREEDY also
+//   records the first position of the maximum in the chunk), the single read
+//   of the vocab. A sequence's units start with its root rows (whose
+//   fixed-point weight sums are also taken, in the sampling modes), then the
+//   other rows in index order, a row's chunks consecutive. Records start as a
+//   sentinel (the launch's memset) that no record value equals.
 // Phase 2 (the block of slice 0, which holds exactly the sequence's root-row
 //   units; nothing waits): walk the tree from the root while the bulk pass
 //   goes on in other blocks.
@@ -15,14 +17,20 @@
 //           equal to it inside that chunk.
 //   STOCH_* the fixed-point softmax statistics (frame c_j = ceil(cmax_j * k),
 //           S_j = sum of weights); then acceptance, residuals and the bonus draw.
-//   Rows other than the root are read again by the walking block for their
-//   chunk maxima and weights, for the rows the walk visits only.
+//   A visited row other than the root needs its records: the walking block
+//   waits (bounded) until they are written, then GREEDY reads no logits at all
+//   and the sampling modes read the row once more for its weights. Should the
+//   wait run out (or when waiting is not allowed: more sequences than SMs),
+//   the block takes the chunk maxima itself from the row; the results are the
+//   same either way.
 // The numbers are exactly those of the oracle (order-independent integer
 // sums), so decisions are bit-exact.
 //
 // Semantics: include/a11spec.h (a11s_accept). Reference behaviour followed:
 // src/engine/speculative_verifier.cpp:84-135 (acceptance rule, first rejection
 // stops the chain), engine/sampler.py:16 (logits / T).
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -78,6 +86,43 @@ __device__ __forceinline__ float chunk_max(const char *row, int c0, int clen, in
             for (int e = 0; e < VT::EPV; ++e) m = max_nan(m, VT::at(d[g], e));
     }
     return warp_max_nan(m);
+}
+
+// Chunk max (as chunk_max) and the first position in the chunk holding it:
+// each lane keeps its running maximum with the first position reaching it
+// (its positions increase along its reads; a NaN never replaces the first
+// value, and a chunk holding a NaN has a NaN maximum whose position is never
+// asked for), then the warp takes the smallest position among the lanes
+// whose maximum equals the chunk's.
+template <bool BF16>
+__device__ __forceinline__ float chunk_max_first(const char *row, int c0, int clen, int lane, int &first) {
+    using VT = Vec<BF16>;
+    constexpr int G = 8;
+    float m = -INFINITY, bv = -INFINITY;
+    int bi = INT_MAX;
+#pragma unroll
+    for (int i0 = 0; i0 < VT::NV; i0 += G) {
+        uint4 d[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < VT::EPV; ++e) {
+                const float v = VT::at(d[g], e);
+                const int pos = ((i0 + g) * 32 + lane) * VT::EPV + e;
+                m = max_nan(m, v);
+                if (pos < clen && (bi == INT_MAX || v > bv)) { bv = v; bi = pos; }
+            }
+    }
+    m = warp_max_nan(m);
+    int f = (bi != INT_MAX && bv == m) ? bi : INT_MAX;
+    first = -warp_max(-f);  // warp min
+    return m;
 }
 
 // Sum of fixed-point weights of one chunk in frame cf (no max needed: the
@@ -236,20 +281,75 @@ __device__ void row_sums(const char *row, int nch, int V, float k, int32_t *fr, 
     if (bad && lane == 0) report(st, A11S_ENONFINITE, b);
 }
 
-// Frames and weight sums of a row: the root's come from the bulk pass (chunk
-// records and weight sums), the others are computed by every warp of the block.
+// As row_sums, with the chunk maxima taken from the row's phase-1 records:
+// one read of the row (its weights) instead of two.
 template <bool BF16>
-__device__ void row_stats_into(const char *row, const float *root_cmax, const unsigned long long *root, int nch,
-                               int V, float k, int32_t *fr, uint64_t *sum, int warp, int lane, StatusWord *st,
-                               int b) {
+__device__ void row_sums_rec(const char *row, const float *rec, int nch, int V, float k, int32_t *fr,
+                             uint64_t *sum, int warp, int lane, StatusWord *st, int b) {
+    int bad = 0;
+    for (int j = warp; j < nch; j += kWarps) {
+        const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+        const float cm = __ldcg(rec + j);
+        bad |= !(cm < INFINITY) || (cm > -INFINITY && !(fabsf(__fmul_rn(cm, k)) < 16777216.0f));
+        const int32_t f = cm < INFINITY ? frame_of(cm, k) : A11S_FRAME_NONE;
+        uint64_t s = 0;
+        if (f != A11S_FRAME_NONE) s = chunk_wsum<BF16>(row, c0, clen, k, (float)f, lane);
+        if (lane == 0) {
+            fr[j] = f;
+            sum[j] = s;
+        }
+    }
+    if (bad && lane == 0) report(st, A11S_ENONFINITE, b);
+}
+
+// Frames and weight sums of a row: the root's come from the bulk pass (chunk
+// records and weight sums); another row's from its chunk records when `rec`
+// is given (the row's counter showed them complete), else the block takes
+// them from the row itself.
+template <bool BF16>
+__device__ void row_stats_into(const char *row, const float *root_cmax, const unsigned long long *root,
+                               const float *rec, int nch, int V, float k, int32_t *fr, uint64_t *sum, int warp,
+                               int lane, StatusWord *st, int b) {
     if (root) {
         for (int j = threadIdx.x; j < nch; j += blockDim.x) {
             fr[j] = frame_of(__ldcg(root_cmax + j), k);
             sum[j] = __ldcg(root + j);
         }
+    } else if (rec) {
+        row_sums_rec<BF16>(row, rec, nch, V, k, fr, sum, warp, lane, st, b);
     } else {
         row_sums<BF16>(row, nch, V, k, fr, sum, warp, lane, st, b);
     }
+}
+
+// Records start as kUnrecorded (the launch's memset); each is written once
+// with its final value, which is never that pattern (max.NaN gives the
+// canonical NaN 0x7FFFFFFF; positions are >= 0). So a record that differs from
+// it is final, and a row is complete when all its records are.
+constexpr uint32_t kUnrecorded = 0xFFFFFFFFu;
+constexpr long long kRecordWaitBudget = 4000000ll;  // ~2 ms of SM clock
+__device__ __forceinline__ void st_relaxed(void *p, uint32_t v) {
+    asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed(const void *p) {
+    uint32_t v;
+    asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+// One record (and its position record, if any) written yet? When waiting is
+// allowed, waits a bounded time: the bulk pass records every live row; on a
+// timeout the caller takes the statistics from the row itself, with the same
+// results.
+__device__ __forceinline__ bool record_ready(const void *rec, const void *pos, bool may_wait) {
+    auto done = [&]() { return ld_relaxed(rec) != kUnrecorded && (!pos || ld_relaxed(pos) != kUnrecorded); };
+    if (done()) return true;
+    if (!may_wait) return false;
+    const long long t0 = clock64();
+    while (!done()) {
+        if (clock64() - t0 > kRecordWaitBudget) return false;
+        __nanosleep(200);
+    }
+    return true;
 }
 
 // Chunk maxima of a row into shared memory (every thread of the block): the
@@ -411,6 +511,24 @@ __device__ int row_argmax(const char *row, const float *cmax, int nch, int V, fl
     return c0 + (first == INT_MAX ? 0 : first);
 }
 
+// Greedy argmax of a row from its records (warp 0): the same choice as
+// row_argmax (first chunk holding the row max; in it, the recorded first
+// position of that max) without reading the row.
+__device__ int row_argmax_rec(const float *cmax, const int32_t *arg, int nch, int lane) {
+    float M = -INFINITY;  // cmax: the row's chunk maxima in shared memory
+    for (int j = lane; j < nch; j += 32) M = fmaxf(M, cmax[j]);
+    M = warp_fmax(M);
+    int jstar = INT_MAX;
+    for (int j0 = 0; j0 < nch && jstar == INT_MAX; j0 += 32) {
+        const int j = j0 + lane;
+        const unsigned hit = __ballot_sync(0xffffffffu, j < nch && cmax[j] == M);
+        if (hit) jstar = j0 + __ffs(hit) - 1;
+    }
+    if (jstar == INT_MAX) return 0;  // every chunk maximum is NaN
+    const int f = __ldcg(arg + jstar);
+    return jstar * A11S_CHUNK + (f == INT_MAX ? 0 : f);
+}
+
 // ---------------------------------------------------------------------------
 // The kernel.
 // ---------------------------------------------------------------------------
@@ -424,10 +542,11 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
 
     // ---------------- phase 1: chunk maxima ----------------
     // Units of a sequence: first the root rows' chunks (the p root, and the q
-    // root in DRAFT mode), then the other rows' chunks, rows fastest. Slice 0
-    // is exactly the root units; its block then walks the tree while the bulk
-    // pass goes on in other blocks: the walk needs the root rows' records and
-    // computes the statistics of the other rows it visits itself.
+    // root in DRAFT mode), then the other rows in index order (p rows 1..N-1,
+    // then q rows 1..N-1), a row's chunks consecutive, so the rows near the
+    // root, which the walk visits first, are recorded first. Slice 0 is
+    // exactly the root units; its block then walks the tree while the bulk
+    // pass goes on in other blocks.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
     const int u0 = blockIdx.y == 0 ? 0 : n_root_units + (blockIdx.y - 1) * a.slice;
@@ -439,9 +558,9 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             j = u / kRootRows;
             r = (u - j * kRootRows) ? a.N : 0;
         } else {
-            const int v = u - n_root_units, other = a.rows_per_seq - kRootRows;
-            j = v / other;
-            const int q = v - j * other;  // 1..N-1 (p rows), then N+1..2N-1 (q rows)
+            const int v = u - n_root_units;
+            const int q = v / a.nch;  // 0..N-2: p rows 1..N-1, then q rows N+1..2N-1
+            j = v - q * a.nch;
             r = q < a.N - 1 ? 1 + q : a.N + 1 + (q - (a.N - 1));
         }
         const bool isq = r >= a.N;
@@ -449,10 +568,16 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         if (node >= n_live) continue;
         const char *row = reinterpret_cast<const char *>(isq ? a.draft : a.target) + ((size_t)b * a.N + node) * row_bytes;
         const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, a.V - c0);
-        const float m = chunk_max<BF16>(row, c0, clen, lane);
+        int first = 0;
+        const float m = MODE == A11S_ACCEPT_GREEDY ? chunk_max_first<BF16>(row, c0, clen, lane, first)
+                                                   : chunk_max<BF16>(row, c0, clen, lane);
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
-        if (lane == 0 && node == 0) a.recs[((size_t)b * kRootRows + (isq ? 1 : 0)) * a.nch + j] = m;
+        const size_t rrow = (size_t)b * a.rows_per_seq + r;
+        if (lane == 0) {  // each record is written once, over the launch's sentinel
+            st_relaxed(a.recs + rrow * a.nch + j, __float_as_uint(m));
+            if (MODE == A11S_ACCEPT_GREEDY) st_relaxed(a.arg + rrow * a.nch + j, (uint32_t)first);
+        }
         if (MODE != A11S_ACCEPT_GREEDY && node == 0) {
             // The walk always starts at the root: its weight sums are taken
             // here, while the chunk is hot in L2, instead of in the walk.
@@ -470,7 +595,19 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     const int N = a.N, V = a.V, nch = a.nch;
     int32_t *an = a.acc_nodes + (size_t)b * N;
     int32_t *at = a.acc_tokens + (size_t)b * N;
-    const float *cmax_b = a.recs + (size_t)b * kRootRows * nch;  // root rows' chunk maxima (p, then q)
+    const float *cmax_b = a.recs + (size_t)b * a.rows_per_seq * nch;  // chunk maxima of the sequence's rows
+    const int32_t *arg_b = MODE == A11S_ACCEPT_GREEDY ? a.arg + (size_t)b * N * nch : nullptr;
+    // Records of row r (p rows 0..N-1, q rows N..2N-1 in DRAFT) if complete,
+    // else null; every thread gets the same answer (thread j < nch checks
+    // chunk j). The root rows' were written by this block before the walk.
+    auto records = [&](int r) -> const float * {
+        const float *rec = cmax_b + (size_t)r * nch;
+        bool mine = true;
+        if ((int)threadIdx.x < nch)
+            mine = record_ready(rec + threadIdx.x, arg_b ? arg_b + (size_t)r * nch + threadIdx.x : nullptr,
+                                a.wait_records != 0);
+        return __syncthreads_and(mine) ? rec : nullptr;
+    };
     const char *tgt_b = reinterpret_cast<const char *>(a.target) + (size_t)b * N * row_bytes;
     const char *drf_b = MODE == A11S_ACCEPT_STOCH_DRAFT
                             ? reinterpret_cast<const char *>(a.draft) + (size_t)b * N * row_bytes
@@ -509,7 +646,8 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             for (int c = r + 1; c < n_live && !has_child; ++c) has_child = sm.par[c] == r;
             if (!has_child) continue;
             const char *prow = tgt_b + (size_t)r * row_bytes;
-            row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, nch, V, a.k,
+            const float *rec = r == 0 ? nullptr : records(r);
+            row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, rec, nch, V, a.k,
                                  sm.fr, sm.sum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
@@ -532,9 +670,11 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         // finds the argmax and the matching child.
         for (;;) {
             const char *row = tgt_b + (size_t)node * row_bytes;
-            row_cmax_into<BF16>(row, node == 0 ? cmax_b : nullptr, nch, V, sm.cmx, warp, lane, a.status, b);
+            const float *rec = node == 0 ? cmax_b : records(node);
+            row_cmax_into<BF16>(row, rec, nch, V, sm.cmx, warp, lane, a.status, b);
             if (warp == 0) {
-                const int am = row_argmax<BF16>(row, sm.cmx, nch, V, sm.cp, lane);
+                const int am = rec ? row_argmax_rec(sm.cmx, arg_b + (size_t)node * nch, nch, lane)
+                                   : row_argmax<BF16>(row, sm.cmx, nch, V, sm.cp, lane);
                 int next = INT_MAX;
                 for (int c0 = node + 1; c0 < n_live && next == INT_MAX; c0 += 32) {
                     const int c = c0 + lane;
@@ -564,9 +704,11 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             const unsigned long long *rs_p = nd == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr;
             const char *prow = tgt_b + (size_t)nd * row_bytes;
             const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
-            row_stats_into<BF16>(prow, cmax_b, rs_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
+            const float *rec_p = nd == 0 ? nullptr : records(nd);
+            const float *rec_q = MODE == A11S_ACCEPT_STOCH_DRAFT && nd != 0 ? records(N + nd) : nullptr;
+            row_stats_into<BF16>(prow, cmax_b, rs_p, rec_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
             if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                row_stats_into<BF16>(qrow, cmax_b + nch, nd == 0 ? rs_p + nch : nullptr, nch, V, a.k,
+                row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, rec_q, nch, V, a.k,
                                      sm.qfr, sm.qsum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
@@ -829,6 +971,22 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     }
     if (failed && warp == 0)
         for (int i = lane; i < N; i += 32) { an[i] = -1; at[i] = -1; }
+}
+
+// Before every acceptance launch: clear the status word and set every record
+// to kUnrecorded (one launch instead of two memsets).
+__global__ void accept_init_kernel(StatusWord *st, uint4 *recs, size_t n16) {
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i0 == 0) *st = StatusWord{};
+    const uint4 u = make_uint4(kUnrecorded, kUnrecorded, kUnrecorded, kUnrecorded);
+    for (size_t i = i0; i < n16; i += (size_t)gridDim.x * blockDim.x) recs[i] = u;
+}
+
+cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, cudaStream_t s) {
+    const size_t n16 = bytes / 16;
+    const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 4 * 148);
+    accept_init_kernel<<<blocks ? blocks : 1, 256, 0, s>>>(st, reinterpret_cast<uint4 *>(recs), n16);
+    return cudaGetLastError();
 }
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s) {

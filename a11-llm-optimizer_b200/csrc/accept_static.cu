@@ -5,8 +5,8 @@
 // (a serving process that budgets every byte of HBM up front), foreign-language
 // bindings without a device allocator of their own, and decode loops that
 // cannot afford cudaMalloc's possible device-wide synchronisation. For them
-// the scratch of the acceptance kernel (status word, the root rows' chunk
-// records and weight sums) lives in one file-scope device array of
+// the scratch of the acceptance kernel (status word, row counters, chunk
+// records and the root rows' weight sums) lives in one file-scope device array of
 // A11S_ACCEPT_STATIC_SCRATCH_BYTES that every GPU loading the library keeps
 // until the process exits. Nothing here calls cudaMalloc, cudaFree or an
 // allocating library routine.
@@ -37,7 +37,7 @@ extern "C" int a11s_accept_static(int32_t mode, int32_t dtype, const void *targe
         char msg[256];
         snprintf(msg, sizeof msg,
                  "a11s_accept_static: needs %zu scratch bytes but the fixed array holds %u "
-                 "(batch * max_nodes * ceil(vocab / 2048) chunk records of 16 bytes); call a11s_accept "
+                 "(8 bytes per row chunk: batch * max_nodes * ceil(vocab / 2048) of them); call a11s_accept "
                  "with a workspace instead",
                  need, (unsigned)A11S_ACCEPT_STATIC_SCRATCH_BYTES);
         return a11s::set_error(A11S_ENOSPACE, msg);
@@ -59,9 +59,9 @@ extern "C" int a11s_accept_static(int32_t mode, int32_t dtype, const void *targe
         }
         scratch = g_scratch_ptr[dev];
     }
-    // a11s_accept clears the status word (the only part that must start at
-    // zero; every record is written before it is read) on the stream before
-    // its kernel runs.
+    // a11s_accept clears the status word and the row counters (the only parts
+    // that must start at zero; every record is written before it is read) on
+    // the stream before its kernel runs.
     const int rc = a11s_accept(mode, dtype, target_logits, draft_logits, row_stride, temperature,
                                uniforms, tokens, parents, n_nodes, batch, max_nodes, vocab,
                                accept_len, accepted_nodes, accepted_tokens, bonus, node_probs,

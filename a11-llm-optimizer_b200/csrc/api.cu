@@ -48,18 +48,20 @@ int sm_count() {
 }
 
 // ---- acceptance workspace layout ----
-// status word | chunk maxima of the root rows [B][root rows][nch] float |
-// weight sums of the root rows [B][2][nch] uint64 (sampling modes)
+// status word (zeroed before each launch) | chunk maxima [B][rows][nch] float |
+// first max positions [B][N][nch] int32 (GREEDY) (both set to 0xFF bytes before
+// each launch) | weight sums of the root rows [B][2][nch] uint64 (sampling
+// modes); rows = max_nodes, or 2 max_nodes in DRAFT (p rows, then q rows)
 struct AcceptLayout {
-    size_t recs, root_sums, total;
+    size_t recs, arg, root_sums, total;
 };
 AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
-    (void)max_nodes;
     AcceptLayout L;
     const size_t nch = (size_t)(vocab + A11S_CHUNK - 1) / A11S_CHUNK;
-    const size_t root_rows = (size_t)batch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    const size_t rows = (size_t)batch * max_nodes * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
     L.recs = kHeaderBytes;
-    L.root_sums = L.recs + up256(root_rows * nch * sizeof(float));
+    L.arg = L.recs + up256(rows * nch * sizeof(float));
+    L.root_sums = L.arg + (mode == A11S_ACCEPT_GREEDY ? up256(rows * nch * sizeof(int32_t)) : 0);
     L.total = L.root_sums + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * 2 * nch * sizeof(uint64_t)));
     return L;
 }
@@ -166,7 +168,12 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     char *ws = static_cast<char *>(workspace);
     a.status = reinterpret_cast<a11s::StatusWord *>(ws);
     a.recs = reinterpret_cast<float *>(ws + L.recs);
+    a.arg = mode == A11S_ACCEPT_GREEDY ? reinterpret_cast<int32_t *>(ws + L.arg) : nullptr;
     a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
+    // A walking block may wait for rows that other blocks record only when the
+    // walkers (one block per sequence, the first ones scheduled) fill at most
+    // half of the 2 resident blocks per SM: the bulk pass always has room.
+    a.wait_records = batch <= sm_count() ? 1 : 0;
 
     // Slice 0 of a sequence is exactly its root rows' units, so that block
     // reads only the root rows before it walks the tree. The other units are
@@ -183,7 +190,7 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     const int grid_y = 1 + (int)((rest + slice - 1) / slice);
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = cudaMemsetAsync(ws, 0, kHeaderBytes, s);  // the status word
+    cudaError_t e = a11s::launch_accept_init(a.status, ws + L.recs, L.root_sums - L.recs, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: clearing workspace");
     e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_y, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: launch");

@@ -23,12 +23,19 @@ struct AcceptArgs {
     int32_t *bonus;
     float *node_probs;
     long long *stats;
-    float *recs;  // [B][root rows: 1, or 2 in DRAFT][nch] chunk maxima of the root rows (NaN-propagating)
+    float *recs;        // [B][rows_per_seq][nch] chunk maxima of every live row (NaN-propagating),
+                        // 0xFFFFFFFF until written; rows are p rows 0..N-1, then q rows (DRAFT)
+    int32_t *arg;       // [B][N][nch] first position of the chunk maximum in the chunk (GREEDY), else
+                        // null; -1 until written
+    int32_t wait_records;  // the walk may wait for other blocks' records: every walking block is
+                           // resident with at least as many slots left for the bulk pass
     unsigned long long *root_sums;  // [B][2][nch] weight sums of the root rows (p, q)
     StatusWord *status;
 };
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s);
+// Clears the status word and marks every record unwritten (bytes: a multiple of 16).
+cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, cudaStream_t s);
 
 struct CompactArgs {
     char *k_pool;
