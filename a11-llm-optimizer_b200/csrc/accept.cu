@@ -187,6 +187,7 @@ struct WalkSmem {
     float kl[A11S_MAX_ACCEPT_NODES];      // their target logits
     float kq[A11S_MAX_ACCEPT_NODES];      // and draft logits (DRAFT)
     float cmx[kMaxNch];     // chunk maxima of the row being visited (GREEDY argmax)
+    int32_t carg[kMaxNch];  // and the first position of each maximum in its chunk
     float cp[A11S_CHUNK];   // one staged chunk of the p row (widened to fp32)
     float cq[A11S_CHUNK];   // and of the q row (DRAFT)
     uint64_t wtot[kWarps];  // per-warp weight totals of the bonus scan
@@ -339,9 +340,14 @@ __device__ __forceinline__ uint32_t ld_relaxed(const void *p) {
 // One record (and its position record, if any) written yet? When waiting is
 // allowed, waits a bounded time: the bulk pass records every live row; on a
 // timeout the caller takes the statistics from the row itself, with the same
-// results.
-__device__ __forceinline__ bool record_ready(const void *rec, const void *pos, bool may_wait) {
-    auto done = [&]() { return ld_relaxed(rec) != kUnrecorded && (!pos || ld_relaxed(pos) != kUnrecorded); };
+// results. The values read are returned in v / pv.
+__device__ __forceinline__ bool record_ready(const void *rec, const void *pos, bool may_wait, uint32_t &v,
+                                             uint32_t &pv) {
+    auto done = [&]() {
+        v = ld_relaxed(rec);
+        pv = pos ? ld_relaxed(pos) : 0u;
+        return v != kUnrecorded && pv != kUnrecorded;
+    };
     if (done()) return true;
     if (!may_wait) return false;
     const long long t0 = clock64();
@@ -511,9 +517,9 @@ __device__ int row_argmax(const char *row, const float *cmax, int nch, int V, fl
     return c0 + (first == INT_MAX ? 0 : first);
 }
 
-// Greedy argmax of a row from its records (warp 0): the same choice as
-// row_argmax (first chunk holding the row max; in it, the recorded first
-// position of that max) without reading the row.
+// Greedy argmax of a row from its records in shared memory (warp 0): the same
+// choice as row_argmax (first chunk holding the row max; in it, the recorded
+// first position of that max) without reading the row.
 __device__ int row_argmax_rec(const float *cmax, const int32_t *arg, int nch, int lane) {
     float M = -INFINITY;  // cmax: the row's chunk maxima in shared memory
     for (int j = lane; j < nch; j += 32) M = fmaxf(M, cmax[j]);
@@ -525,7 +531,7 @@ __device__ int row_argmax_rec(const float *cmax, const int32_t *arg, int nch, in
         if (hit) jstar = j0 + __ffs(hit) - 1;
     }
     if (jstar == INT_MAX) return 0;  // every chunk maximum is NaN
-    const int f = __ldcg(arg + jstar);
+    const int f = arg[jstar];
     return jstar * A11S_CHUNK + (f == INT_MAX ? 0 : f);
 }
 
@@ -600,12 +606,19 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // Records of row r (p rows 0..N-1, q rows N..2N-1 in DRAFT) if complete,
     // else null; every thread gets the same answer (thread j < nch checks
     // chunk j). The root rows' were written by this block before the walk.
+    // GREEDY also gets the values in shared memory (sm.cmx, sm.carg).
     auto records = [&](int r) -> const float * {
         const float *rec = cmax_b + (size_t)r * nch;
         bool mine = true;
-        if ((int)threadIdx.x < nch)
+        if ((int)threadIdx.x < nch) {
+            uint32_t v, pv;
             mine = record_ready(rec + threadIdx.x, arg_b ? arg_b + (size_t)r * nch + threadIdx.x : nullptr,
-                                a.wait_records != 0);
+                                a.wait_records != 0, v, pv);
+            if (MODE == A11S_ACCEPT_GREEDY) {
+                sm.cmx[threadIdx.x] = __uint_as_float(v);
+                sm.carg[threadIdx.x] = (int32_t)pv;
+            }
+        }
         return __syncthreads_and(mine) ? rec : nullptr;
     };
     const char *tgt_b = reinterpret_cast<const char *>(a.target) + (size_t)b * N * row_bytes;
@@ -670,10 +683,12 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         // finds the argmax and the matching child.
         for (;;) {
             const char *row = tgt_b + (size_t)node * row_bytes;
-            const float *rec = node == 0 ? cmax_b : records(node);
-            row_cmax_into<BF16>(row, rec, nch, V, sm.cmx, warp, lane, a.status, b);
+            // the row's chunk maxima and first positions, staged by records()
+            // (the root's were written by this block), else taken from the row
+            const bool rec = records(node) != nullptr;
+            if (!rec) row_cmax_into<BF16>(row, nullptr, nch, V, sm.cmx, warp, lane, a.status, b);
             if (warp == 0) {
-                const int am = rec ? row_argmax_rec(sm.cmx, arg_b + (size_t)node * nch, nch, lane)
+                const int am = rec ? row_argmax_rec(sm.cmx, sm.carg, nch, lane)
                                    : row_argmax<BF16>(row, sm.cmx, nch, V, sm.cp, lane);
                 int next = INT_MAX;
                 for (int c0 = node + 1; c0 < n_live && next == INT_MAX; c0 += 32) {
