@@ -120,6 +120,31 @@ def test_stochastic_onehot_vs_oracle(dtype, T):
             assert abs(r["node_probs"][b, i] - ref) <= 1e-5 * ref + 1e-9
 
 
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_walk_with_and_without_waiting_for_records(mode):
+    """Up to one sequence per SM, the walk waits for the rows that other blocks
+    record; above that it takes a visited row's statistics from the row itself.
+    Both give the oracle's decisions, on deep walks (forced matches) and a
+    ragged last chunk."""
+    n_sms = torch.cuda.get_device_properties(0).multi_processor_count
+    N, V = 12, 2 * 2048 + 136
+    for B in (3, n_sms + 52):
+        rng = np.random.default_rng(31 + mode + B)
+        x = rng.normal(0, 2, (B, N, V)).astype(np.float32)
+        parents = np.stack([W.random_parents(N, rng) for _ in range(B)]).astype(np.int32)
+        tokens = rng.integers(0, V, (B, N)).astype(np.int32)
+        for b in range(B):
+            for i in range(1, N):
+                if rng.random() < 0.7:
+                    x[b, parents[b, i], tokens[b, i]] += 40.0
+        q = (x + rng.normal(0, 0.5, x.shape)).astype(np.float32) if mode == 2 else None
+        uni = rng.random((B, N), dtype=np.float32) if mode else None
+        r = run_gpu(mode, x, tokens, parents, draft=q, T=0.8, uniforms=uni)
+        o = oracle.accept(mode, x, tokens, parents, draft=q, temperature=0.8, uniforms=uni)
+        assert_same_decisions(r, o)
+        assert r["accept_len"].mean() > 1.0, B  # the walks leave the root
+
+
 def test_c3_draft_logits_reduced_vs_oracle():
     d = W.make_c3(seed=3, batch=3, n_nodes=64, vocab=151936)
     r = run_gpu(2, d["p"], d["tokens"], d["parents"], d["n_nodes"], draft=d["q"],
