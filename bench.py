@@ -165,8 +165,8 @@ def run_ours(args, rank, world, local_rank):
     attn_out = torch.empty_like(q)
     attn_ws = a11spec.ops.workspace(a11spec.ops.tree_attention_workspace_bytes(B, MAX_NODES, HQ, HKV, D, max_kv), dev)
     # liba11spec kernels per step: n-gram expand, page reserve, tree attention (+ split combine),
-    # accept, compaction (2), page release
-    launches_per_step = 7 + (1 if attn_ws.numel() > 256 else 0)
+    # accept (record init + accept), compaction (2), page release
+    launches_per_step = 8 + (1 if attn_ws.numel() > 256 else 0)
     logits = torch.empty(B * MAX_NODES, VOCAB, dtype=torch.bfloat16, device=dev)
     uni = torch.empty(B, MAX_NODES, dtype=torch.float32, device=dev)
     acc = a11spec.ops.alloc_accept(a11spec.STOCH_ONEHOT, B, MAX_NODES, VOCAB, dev)
