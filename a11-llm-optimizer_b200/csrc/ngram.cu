@@ -1,10 +1,11 @@
 // ngram.cu - K1: hashed trigram table lookup expanding a draft token tree.
 //
 // One warp per sequence, one tree level per round: each lane owns one node of
-// the level, reads its bucket (slots x 8 bytes), selects its top-w
-// continuations by count in registers, and a warp prefix sum places the
+// the level, reads its bucket (slots x 8 bytes, 16-byte loads), selects its
+// top-w continuations by count in registers, and a warp prefix sum places the
 // children in breadth-first order (parents in index order, children by rank),
-// stopping at max_nodes. A tree of depth D costs D dependent bucket reads.
+// stopping at max_nodes. The tree grows in shared memory and is written out
+// once. A tree of depth D costs D dependent bucket reads.
 // Semantics: include/a11spec.h (a11s_ngram_expand); the key is the last two
 // tokens, as engine/speculative.py:21 of the reference.
 #include "common.cuh"
@@ -21,38 +22,49 @@ __device__ __forceinline__ uint32_t bucket_of(int32_t a, int32_t b, int log2_buc
 }
 
 constexpr int kNgramWarps = 4;
+static_assert(kNgramWarps * 3 * A11S_MAX_NODES * sizeof(int32_t) <= 48 * 1024,
+              "the per-warp trees fit the default dynamic shared memory");
 
 __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const NgramArgs a) {
+    extern __shared__ int32_t ng_tree[];  // per warp: tokens, parents, depths [max_nodes] each
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x * kNgramWarps + warp;
     if (b >= a.B) return;
-    int32_t *tk = a.tokens + (size_t)b * a.max_nodes;
-    int32_t *pa = a.parents + (size_t)b * a.max_nodes;
-    int32_t *de = a.depths + (size_t)b * a.max_nodes;
-    for (int i = lane; i < a.max_nodes; i += 32) { tk[i] = -1; pa[i] = -1; de[i] = -1; }
-    __syncwarp();
+    const int M = a.max_nodes;
+    // The tree grows in shared memory (each level reads the tokens of the one
+    // before) and is written out once at the end.
+    int32_t *stk = ng_tree + (size_t)warp * 3 * M, *spa = stk + M, *sde = spa + M;
     const int32_t prev0 = a.last_tokens[2 * b], root = a.last_tokens[2 * b + 1];
-    if (lane == 0) { tk[0] = root; de[0] = 0; }
+    if (lane == 0) { stk[0] = root; spa[0] = -1; sde[0] = 0; }
     __syncwarp();
+    // 16-byte bucket reads (two slots each) when the table allows them
+    const bool vec = (a.slots & 1) == 0 && (reinterpret_cast<uintptr_t>(a.table) & 15) == 0;
     int n = 1, lvl_start = 0, lvl_end = 1, depth = 0;
-    while (lvl_start < lvl_end && n < a.max_nodes && depth < a.max_depth) {
+    while (lvl_start < lvl_end && n < M && depth < a.max_depth) {
         const int w = depth == 0 ? a.width_root : a.width_inner;
-        for (int g = lvl_start; g < lvl_end && n < a.max_nodes; g += 32) {
+        for (int g = lvl_start; g < lvl_end && n < M; g += 32) {
             const int i = g + lane;
             int sel_tok[32];
             int cnt = 0;
             if (i < lvl_end) {
-                const int32_t t = tk[i];
-                const int32_t prev = i == 0 ? prev0 : tk[pa[i]];
+                const int32_t t = stk[i];
+                const int32_t prev = i == 0 ? prev0 : stk[spa[i]];
                 const int32_t *bk = a.table + (size_t)bucket_of(prev, t, a.log2_buckets) * a.slots * 2;
                 int32_t st[32], sc[32];
-                for (int s = 0; s < a.slots; ++s) { st[s] = __ldg(bk + 2 * s); sc[s] = __ldg(bk + 2 * s + 1); }
+                if (vec) {
+                    for (int s2 = 0; s2 < a.slots; s2 += 2) {
+                        const int4 v = __ldg(reinterpret_cast<const int4 *>(bk + 2 * s2));
+                        st[s2] = v.x; sc[s2] = v.y; st[s2 + 1] = v.z; sc[s2 + 1] = v.w;
+                    }
+                } else {
+                    for (int s2 = 0; s2 < a.slots; ++s2) { st[s2] = __ldg(bk + 2 * s2); sc[s2] = __ldg(bk + 2 * s2 + 1); }
+                }
                 unsigned used = 0;
                 for (int r = 0; r < w; ++r) {
                     int best = -1;
-                    for (int s = 0; s < a.slots; ++s) {
-                        if (((used >> s) & 1u) || sc[s] <= 0) continue;
-                        if (best < 0 || sc[s] > sc[best]) best = s;
+                    for (int s2 = 0; s2 < a.slots; ++s2) {
+                        if (((used >> s2) & 1u) || sc[s2] <= 0) continue;
+                        if (best < 0 || sc[s2] > sc[best]) best = s2;
                     }
                     if (best < 0) break;
                     used |= 1u << best;
@@ -69,20 +81,30 @@ __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const Ng
             const int base = n + incl - cnt;
             for (int r = 0; r < cnt; ++r) {
                 const int idx = base + r;
-                if (idx < a.max_nodes) { tk[idx] = sel_tok[r]; pa[idx] = i; de[idx] = depth + 1; }
+                if (idx < M) { stk[idx] = sel_tok[r]; spa[idx] = i; sde[idx] = depth + 1; }
             }
-            n = min(a.max_nodes, n + __shfl_sync(0xffffffffu, incl, 31));
+            n = min(M, n + __shfl_sync(0xffffffffu, incl, 31));
             __syncwarp();
         }
         lvl_start = lvl_end;
         lvl_end = n;
         ++depth;
     }
+    int32_t *tk = a.tokens + (size_t)b * M;
+    int32_t *pa = a.parents + (size_t)b * M;
+    int32_t *de = a.depths + (size_t)b * M;
+    for (int i = lane; i < M; i += 32) {
+        const bool in = i < n;
+        tk[i] = in ? stk[i] : -1;
+        pa[i] = in ? spa[i] : -1;
+        de[i] = in ? sde[i] : -1;
+    }
     if (lane == 0) a.n_nodes[b] = n;
 }
 
 cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s) {
-    ngram_expand_kernel<<<(a.B + kNgramWarps - 1) / kNgramWarps, kNgramWarps * 32, 0, s>>>(a);
+    const size_t smem = (size_t)kNgramWarps * 3 * a.max_nodes * sizeof(int32_t);  // <= 48 KB for max_nodes <= 1024
+    ngram_expand_kernel<<<(a.B + kNgramWarps - 1) / kNgramWarps, kNgramWarps * 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 
