@@ -176,10 +176,18 @@ def run_ours(args, rank, world, local_rank):
     grown = torch.empty(B, dtype=torch.int32, device=dev)
     ev_attn = []
 
-    def step(timed_events=None, inputs=None):
+    def step(timed_events=None, inputs=None, ready=None):
         # inputs: (hidden, q, last, uniforms) of this step; default the resident
-        # set with uniforms drawn on the device
+        # set with uniforms drawn on the device. ready: events of the copies of
+        # (last, q, hidden, uniforms); each input is waited for just before its
+        # first use, so a step starts while its later inputs are still copying.
         hid, qq, lst, un = (hidden, q, last, None) if inputs is None else inputs
+
+        def wait(j):
+            if ready is not None:
+                torch.cuda.current_stream().wait_event(ready[j])
+
+        wait(0)
         tk, pa, de, nn = a11spec.ngram_expand(table, lst, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES, out=tree)
         grown.copy_(ctx_lens)
         pages.reserve(page_table, grown, nn)  # pages for the tree slots ctx_lens + i
@@ -187,12 +195,15 @@ def run_ours(args, rank, world, local_rank):
             e0 = torch.cuda.Event(enable_timing=True)
             e1 = torch.cuda.Event(enable_timing=True)
             e0.record()
+        wait(1)
         a11spec.tree_attention(qq, k_pool, v_pool, page_table, ctx_lens, pa, nn, max_kv_len=max_kv,
                                out=attn_out, ws=attn_ws)
         if timed_events is not None:
             e1.record()
             timed_events.append((e0, e1))
+        wait(2)
         torch.matmul(hid, w, out=logits)
+        wait(3)
         if un is None:
             uni.uniform_(generator=gen)
             un = uni
@@ -244,22 +255,24 @@ def run_ours(args, rank, world, local_rank):
     bo = sum(t.numel() * t.element_size() for t in (h_out_tok, h_out_len, h_out_bonus))
 
     # Two input sets: step k+1's H2D runs on a copy stream while step k
-    # computes (a serving loop's double buffering); step k waits for its own
-    # copy, and a set is refilled only after the step that read it.
+    # computes (a serving loop's double buffering); step k waits for each of
+    # its inputs just before the first kernel that reads it, and a set is
+    # refilled only after the step that read it.
     copy_stream = torch.cuda.Stream(device=dev)
     ins = [(hidden, q, last, torch.empty_like(uni)),
            (hidden.clone(), q.clone(), last.clone(), torch.empty_like(uni))]
-    ready = [torch.cuda.Event(), torch.cuda.Event()]
+    ready = [[torch.cuda.Event() for _ in range(4)] for _ in range(2)]  # per set: last, q, hidden, uniforms
     free = [torch.cuda.Event(), torch.cuda.Event()]
 
     def h2d(k):
-        dst = ins[k % 2]
+        hid_d, q_d, last_d, uni_d = ins[k % 2]
         with torch.cuda.stream(copy_stream):
             if k >= 2:
                 copy_stream.wait_event(free[k % 2])
-            for d_, h_ in zip(dst, (h_hidden, h_q, h_last, h_uni)):
+            # in order of first use, each with its own event
+            for j, (d_, h_) in enumerate(((last_d, h_last), (q_d, h_q), (hid_d, h_hidden), (uni_d, h_uni))):
                 d_.copy_(h_, non_blocking=True)
-            ready[k % 2].record(copy_stream)
+                ready[k % 2][j].record(copy_stream)
 
     def e2e_run(n):
         copy_stream.wait_stream(torch.cuda.current_stream())  # copies start after the timing event
@@ -267,8 +280,7 @@ def run_ours(args, rank, world, local_rank):
         for k in range(n):
             if k + 1 < n:
                 h2d(k + 1)
-            torch.cuda.current_stream().wait_event(ready[k % 2])
-            step(inputs=ins[k % 2])
+            step(inputs=ins[k % 2], ready=ready[k % 2])
             free[k % 2].record()
             h_out_tok.copy_(acc.accepted_tokens, non_blocking=True)
             h_out_len.copy_(acc.accept_len, non_blocking=True)
