@@ -63,13 +63,15 @@ def _load() -> C.CDLL:
     lib.a11s_accept_static.argtypes = [i32, i32, vp, vp, i64, f32, vp, vp, vp, vp, i32, i32, i32,
                                        vp, vp, vp, vp, vp, vp, vp, vp]
     lib.a11s_ngram_update.argtypes = [vp, i32, i32, vp, i32, vp, i32, vp, vp]
+    lib.a11s_next_roots.argtypes = [vp, vp, vp, vp, i32, i32, vp, vp, i32, vp, vp]
     lib.a11s_kv_pool_init.argtypes = [vp, vp, i32, vp]
     lib.a11s_kv_reserve.argtypes = [vp, vp, i32, vp, i32, vp, vp, i32, vp, vp]
     lib.a11s_kv_release.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, vp]
     lib.a11s_kv_free_sequences.argtypes = [vp, vp, i32, vp, i32, vp, vp, i32, vp, vp]
     for name in ("a11s_read_status", "a11s_accept", "a11s_tree_attention", "a11s_kv_compact",
                  "a11s_ngram_expand", "a11s_verify_chain", "a11s_accept_static", "a11s_kv_pool_init",
-                 "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update"):
+                 "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update",
+                 "a11s_next_roots"):
         getattr(lib, name).restype = C.c_int
     if lib.a11s_abi_version() != 1:
         raise ImportError("liba11spec.so ABI version mismatch")
@@ -90,4 +92,5 @@ def symbols():
             "a11s_accept_workspace_bytes", "a11s_accept", "a11s_accept_static",
             "a11s_tree_attention_workspace_bytes", "a11s_tree_attention", "a11s_kv_compact",
             "a11s_ngram_expand", "a11s_ngram_bucket", "a11s_verify_chain", "a11s_kv_pool_init",
-            "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update"]
+            "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update",
+            "a11s_next_roots"]

@@ -72,14 +72,12 @@ def speculative_stream(model, prompts: torch.Tensor, max_new_tokens: int, decode
         freed, n_freed = ops.kv_compact(model.k_pool, model.v_pool, page_table, ctx_lens, res.accept_len,
                                         res.accepted_nodes, tree.n_nodes)
         pages.release(freed, n_freed)
+        # next root pair (last accepted token, or the old root; bonus) and, when
+        # learning, the committed-token rows built from the old pair: one launch
+        ops.next_roots(tree.tokens, res.accepted_tokens, res.accept_len, res.bonus, last,
+                       history=hist_buf if learn else None)
         if learn:
-            hist, hlen = ops.history_from_accept(last, res.accepted_tokens, res.accept_len, res.bonus, out=hist_buf)
-            ops.ngram_update(decoder.table, hist, hlen, decoder.log2_buckets, status=status)
-        # next root pair: (last accepted token, or the old root; bonus)
-        idx = (res.accept_len.long() - 1).clamp_min(0).unsqueeze(1)
-        prev = torch.where(res.accept_len > 0, res.accepted_tokens.gather(1, idx).squeeze(1), tree.tokens[:, 0])
-        last[:, 0].copy_(prev)
-        last[:, 1].copy_(res.bonus.clamp_min(0))
+            ops.ngram_update(decoder.table, hist_buf[0], hist_buf[1], decoder.log2_buckets, status=status)
         alen = res.accept_len.cpu().tolist()
         toks = res.accepted_tokens.cpu().tolist()
         bonus = res.bonus.cpu().tolist()

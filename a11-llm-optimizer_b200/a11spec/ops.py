@@ -299,6 +299,34 @@ def history_from_accept(last_tokens: torch.Tensor, accepted_tokens: torch.Tensor
     return hist, lens_out
 
 
+def next_roots(tree_tokens: torch.Tensor, accepted_tokens: torch.Tensor, accept_len: torch.Tensor,
+               bonus: torch.Tensor, last_tokens: torch.Tensor, history=None):
+    """One launch after an acceptance step (a11s_next_roots): last_tokens int32
+    [B, 2] becomes the next tree's root pair (last accepted token, or the old
+    root; the bonus, 0 if none), in place. With `history` = (rows int32
+    [B, >= N + 3], lens int32 [B]) it also writes the committed-token rows for
+    ngram_update from the old pair, as history_from_accept does. Returns
+    `history` (or None)."""
+    B, N = accepted_tokens.shape
+    for t, name in ((tree_tokens, "tree_tokens"), (accepted_tokens, "accepted_tokens"), (accept_len, "accept_len"),
+                    (bonus, "bonus"), (last_tokens, "last_tokens")):
+        _need(t, name, torch.int32)
+    if tuple(tree_tokens.shape) != (B, N) or tuple(last_tokens.shape) != (B, 2):
+        raise ValueError("next_roots: tree_tokens [B, N] and last_tokens [B, 2] expected")
+    rows = lens = None
+    if history is not None:
+        rows, lens = history
+        _need(rows, "history", torch.int32)
+        _need(lens, "history lens", torch.int32)
+        if rows.shape[0] != B or rows.shape[1] < N + 3 or lens.numel() != B:
+            raise ValueError("next_roots: history rows [B, >= N + 3] and lens [B] expected")
+    check(lib.a11s_next_roots(_ptr(tree_tokens), _ptr(accepted_tokens), _ptr(accept_len), _ptr(bonus), B, N,
+                              _ptr(last_tokens), _ptr(rows) if rows is not None else None,
+                              rows.shape[1] if rows is not None else 0, _ptr(lens) if lens is not None else None,
+                              _stream()))
+    return history
+
+
 def ngram_update(table: torch.Tensor, history: torch.Tensor, lens: torch.Tensor, log2_buckets: int,
                  status: Optional[torch.Tensor] = None, check_status: bool = False) -> torch.Tensor:
     """K6, in place on table int32 [2^k, slots, 2]: adds the trigrams of each

@@ -320,6 +320,22 @@ int a11s_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const
     return A11S_OK;
 }
 
+int a11s_next_roots(const int32_t *tree_tokens, const int32_t *accepted_tokens, const int32_t *accept_len,
+                    const int32_t *bonus, int32_t batch, int32_t max_nodes, int32_t *last_tokens, int32_t *history,
+                    int32_t history_stride, int32_t *history_len, void *stream) {
+    if (batch < 0 || max_nodes < 1) return fail(A11S_EINVAL, "a11s_next_roots: batch %d / max_nodes %d", batch, max_nodes);
+    if (history && history_stride < max_nodes + 3)
+        return fail(A11S_EINVAL, "a11s_next_roots: history_stride %d < max_nodes + 3", history_stride);
+    if (batch == 0) return A11S_OK;
+    if (!tree_tokens || !accepted_tokens || !accept_len || !bonus || !last_tokens || (history && !history_len))
+        return fail(A11S_EINVAL, "a11s_next_roots: null required pointer");
+    a11s::NextRootsArgs a{tree_tokens, accepted_tokens, accept_len, bonus, batch, max_nodes, last_tokens, history,
+                          history_stride, history_len};
+    cudaError_t e = a11s::launch_next_roots(a, reinterpret_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_next_roots: launch");
+    return A11S_OK;
+}
+
 // ------------------------------------------------------------------- K5
 int a11s_kv_pool_init(int32_t *free_stack, int32_t *free_top, int32_t num_pages, void *stream) {
     if (num_pages < 0) return fail(A11S_EINVAL, "a11s_kv_pool_init: num_pages %d < 0", num_pages);

@@ -80,6 +80,17 @@ struct NgramUpdateArgs {
 
 cudaError_t launch_ngram_update(const NgramUpdateArgs &a, cudaStream_t s);
 
+struct NextRootsArgs {
+    const int32_t *tree_tokens, *accepted_tokens, *accept_len, *bonus;  // [B][N], [B][N], [B], [B]
+    int32_t B, N;
+    int32_t *last_tokens;              // [B][2], updated in place
+    int32_t *history;                  // [B][history_stride] or null
+    int32_t history_stride;
+    int32_t *history_len;              // [B] (with history)
+};
+
+cudaError_t launch_next_roots(const NextRootsArgs &a, cudaStream_t s);
+
 struct KvPagesArgs {
     int32_t *free_stack, *free_top;  // LIFO of free page ids, entries [0, *free_top)
     int32_t num_pages;

@@ -227,4 +227,44 @@ cudaError_t launch_ngram_update(const NgramUpdateArgs &a, cudaStream_t s) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// After an acceptance step, per sequence (one warp): the committed-token row
+// for K6 (old root pair, accepted tokens, bonus, then -1) and the next tree's
+// root pair (last accepted token, or the old root when nothing was accepted;
+// the bonus, 0 if none). The old pair is read by every lane before lane 0
+// overwrites it.
+// ---------------------------------------------------------------------------
+__global__ void next_roots_kernel(const NextRootsArgs a) {
+    const int b = (int)((blockIdx.x * blockDim.x + threadIdx.x) >> 5), lane = threadIdx.x & 31;
+    if (b >= a.B) return;
+    const int N = a.N;
+    const int32_t *acc = a.accepted_tokens + (size_t)b * N;
+    const int alen = min(max(a.accept_len[b], 0), N);
+    const int32_t bonus = a.bonus[b];
+    const int32_t old0 = a.last_tokens[2 * b], old1 = a.last_tokens[2 * b + 1];
+    if (a.history) {
+        int32_t *h = a.history + (size_t)b * a.history_stride;
+        for (int i = lane; i < a.history_stride; i += 32) {
+            int32_t v = -1;
+            if (i == 0) v = old0;
+            else if (i == 1) v = old1;
+            else if (i - 2 < alen) v = acc[i - 2];
+            else if (i - 2 == alen) v = bonus;
+            h[i] = v;
+        }
+        if (lane == 0) a.history_len[b] = alen + 3;
+    }
+    __syncwarp();
+    if (lane == 0) {
+        a.last_tokens[2 * b] = alen > 0 ? acc[alen - 1] : a.tree_tokens[(size_t)b * N];
+        a.last_tokens[2 * b + 1] = bonus < 0 ? 0 : bonus;
+    }
+}
+
+cudaError_t launch_next_roots(const NextRootsArgs &a, cudaStream_t s) {
+    const unsigned blocks = (unsigned)((a.B + 7) / 8);  // 8 sequences (warps) per block
+    next_roots_kernel<<<blocks, 256, 0, s>>>(a);
+    return cudaGetLastError();
+}
+
 }  // namespace a11s

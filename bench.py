@@ -165,8 +165,8 @@ def run_ours(args, rank, world, local_rank):
     attn_out = torch.empty_like(q)
     attn_ws = a11spec.ops.workspace(a11spec.ops.tree_attention_workspace_bytes(B, MAX_NODES, HQ, HKV, D, max_kv), dev)
     # liba11spec kernels per step: n-gram expand, page reserve, tree attention (+ split combine),
-    # accept (record init + accept), compaction (2), page release
-    launches_per_step = 8 + (1 if attn_ws.numel() > 256 else 0)
+    # accept (record init + accept), compaction (2), page release, next roots
+    launches_per_step = 9 + (1 if attn_ws.numel() > 256 else 0)
     logits = torch.empty(B * MAX_NODES, VOCAB, dtype=torch.bfloat16, device=dev)
     uni = torch.empty(B, MAX_NODES, dtype=torch.float32, device=dev)
     acc = a11spec.ops.alloc_accept(a11spec.STOCH_ONEHOT, B, MAX_NODES, VOCAB, dev)
@@ -213,10 +213,7 @@ def run_ours(args, rank, world, local_rank):
                            nn, freed_pages=freed, n_freed=n_freed, ws=kv_ws)
         pages.release(freed, n_freed)
         # next root pair: (last accepted token or old root, bonus)
-        idx = (acc.accept_len.long() - 1).clamp_min(0).unsqueeze(1)
-        prev = torch.where(acc.accept_len > 0, acc.accepted_tokens.gather(1, idx).squeeze(1), tk[:, 0])
-        lst[:, 0].copy_(prev)
-        lst[:, 1].copy_(acc.bonus.clamp_min(0))
+        a11spec.next_roots(tk, acc.accepted_tokens, acc.accept_len, acc.bonus, lst)
         if world > 1:
             torch.distributed.all_reduce(stats.clone(), op=torch.distributed.ReduceOp.SUM)
 

@@ -12,6 +12,7 @@
  *   a11s_kv_reserve / a11s_kv_release / a11s_kv_free_sequences
  *                         the page allocator of the paged KV cache    (K5)
  *   a11s_ngram_update     the n-gram table learns committed tokens    (K6)
+ *   a11s_next_roots       next roots and committed-token rows of a step (K6 input)
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are caller-owned DEVICE pointers, row-major and
@@ -343,6 +344,23 @@ uint32_t a11s_ngram_bucket(int32_t a, int32_t b, int32_t log2_buckets);
 int a11s_ngram_update(int32_t *table, int32_t log2_buckets, int32_t slots, const int32_t *history,
                       int32_t history_stride, const int32_t *history_len, int32_t batch, int32_t *status,
                       void *stream);
+
+/* The decode loop's hand-over from one speculative step to the next, the role
+ * of the reference's sample -> forward_token feed (engine/pipeline.py:491-503):
+ * per sequence b, after a11s_accept,
+ *   last_tokens[b] <- (accepted_tokens[b][alen - 1], or tree_tokens[b][0] (the
+ *                      old root) when alen = 0;  max(bonus[b], 0))
+ * and, when `history` is not NULL, the committed-token row for
+ * a11s_ngram_update, built from the OLD pair:
+ *   history[b] = (last_tokens[b][0], last_tokens[b][1], accepted_tokens[b][0 .. alen),
+ *                 bonus[b], then -1 up to history_stride), history_len[b] = alen + 3,
+ * with alen = accept_len[b] clamped to [0, max_nodes]. last_tokens int32 [batch][2]
+ * is updated in place; tree_tokens and accepted_tokens are [batch][max_nodes];
+ * history_stride >= max_nodes + 3. One launch, one warp per sequence.
+ */
+int a11s_next_roots(const int32_t *tree_tokens, const int32_t *accepted_tokens, const int32_t *accept_len,
+                    const int32_t *bonus, int32_t batch, int32_t max_nodes, int32_t *last_tokens, int32_t *history,
+                    int32_t history_stride, int32_t *history_len, void *stream);
 
 #ifdef __cplusplus
 }

@@ -74,3 +74,31 @@ def test_accept_then_learn_then_draft(dev):
     want = [[100, 101, 102, 900], [200, 201, 901], [300, 902], [903]]
     for b in range(B):
         assert tk[b, 1:1 + len(want[b])].tolist() == want[b], (b, tk[b].tolist())
+
+
+@pytest.mark.parametrize("with_history", [True, False])
+def test_next_roots_matches_host_ops(dev, with_history):
+    """a11s_next_roots gives the same next root pair and committed-token rows as
+    the torch composition it replaces (history_from_accept, gather/where), for
+    accept lengths 0..N, and bonus -1 (nothing drawn) included."""
+    g = torch.Generator().manual_seed(5)
+    B, N, V = 37, 16, 5000
+    alen = torch.randint(0, N + 1, (B,), generator=g, dtype=torch.int32)
+    alen[:3] = torch.tensor([0, N, 1], dtype=torch.int32)
+    acc = torch.randint(0, V, (B, N), generator=g, dtype=torch.int32)
+    acc[torch.arange(N).unsqueeze(0) >= alen.unsqueeze(1)] = -1  # a11s_accept's layout: -1 past accept_len
+    bonus = torch.randint(-1, V, (B,), generator=g, dtype=torch.int32)
+    tree = torch.randint(0, V, (B, N), generator=g, dtype=torch.int32)
+    last = torch.randint(0, V, (B, 2), generator=g, dtype=torch.int32)
+    acc, alen, bonus, tree, last_d = (t.to(dev) for t in (acc, alen, bonus, tree, last))
+    want_hist, want_len = history_from_accept(last_d, acc, alen, bonus)
+    idx = (alen.long() - 1).clamp_min(0).unsqueeze(1)
+    want_last = torch.stack([torch.where(alen > 0, acc.gather(1, idx).squeeze(1), tree[:, 0]),
+                             bonus.clamp_min(0)], dim=1)
+    hist = (torch.full((B, N + 3), 7, dtype=torch.int32, device=dev), torch.zeros(B, dtype=torch.int32, device=dev))
+    a11spec.next_roots(tree, acc, alen, bonus, last_d, history=hist if with_history else None)
+    torch.cuda.synchronize()
+    assert torch.equal(last_d, want_last)
+    if with_history:
+        assert torch.equal(hist[0], want_hist)
+        assert torch.equal(hist[1], want_len)
