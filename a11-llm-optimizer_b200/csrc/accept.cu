@@ -259,10 +259,10 @@ __device__ RowStat combine_sums(const int32_t *fr, const uint64_t *sum, int nch,
 }
 
 // Every warp of the block: frames and weight sums of one non-root row into
-// fr/sum. The row's chunk maxima are taken here (the bulk pass keeps only the
-// root rows' records), then each chunk's weights in its frame (a second read
-// of the chunk, from L2). A non-finite logit or an out-of-range frame is
-// reported like in the bulk pass.
+// fr/sum, when the row's records are not available (see records() in the
+// kernel). The row's chunk maxima are taken here, then each chunk's weights in
+// its frame (a second read of the chunk, from L2). A non-finite logit or an
+// out-of-range frame is reported like in the bulk pass.
 template <bool BF16>
 __device__ void row_sums(const char *row, int nch, int V, float k, int32_t *fr, uint64_t *sum, int warp, int lane,
                          StatusWord *st, int b) {
@@ -679,8 +679,9 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     int alen = 0, node = 0, bonus = -1;
     bool failed = false;
     if (MODE == A11S_ACCEPT_GREEDY) {
-        // Every warp takes the chunk maxima of a visited non-root row; warp 0
-        // finds the argmax and the matching child.
+        // Per visited node: its chunk maxima and first positions (records, or
+        // taken from the row by every warp); warp 0 finds the argmax and the
+        // matching child.
         for (;;) {
             const char *row = tgt_b + (size_t)node * row_bytes;
             // the row's chunk maxima and first positions, staged by records()

@@ -101,8 +101,8 @@ int a11s_read_status(const void *workspace, int32_t *status, int32_t *detail, vo
  * (engine/speculative.py:26-34) and tree_rejection_kernel (src/cuda/tree_verification.cu:71-101).
  *
  * One kernel reads every logits row once (vectorised, warp-shuffle reductions
- * over 2048-token chunks), and the block that completes a sequence's root row
- * walks its tree from the root: at each accepted node the children are tried in index
+ * over 2048-token chunks, recording each chunk's maximum), and the block that
+ * reads a sequence's root row walks its tree from the root: at each accepted node the children are tried in index
  * order; the first accepted child becomes the next node; when none is accepted
  * (or the node is a leaf) the bonus token is drawn at that node.
  *
