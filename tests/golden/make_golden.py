@@ -5,6 +5,14 @@ verifier (oracle/_ref, from src/engine/speculative_verifier.cpp) and records
 its decisions, so the committed JSON pins the oracle and the kernels to the
 reference on machines without it.
 
+attn_chains.npz comes from the reference's decode attention itself: its paged
+KV cache class (engine/kv_cache.py, KVCacheManager.append / get_kv) holds the
+keys and values, and the attention statements of A11Pipeline.forward_layer
+(engine/pipeline.py, from the "Grouped Query Attention" comment to attn_out)
+are read from that file at generation time and executed on the tensors. A
+chain-shaped draft tree is exactly the reference's token-by-token decode: node
+i attends to the context and nodes 0..i.
+
     python tests/golden/make_golden.py
 """
 import json
@@ -66,6 +74,54 @@ def ref_chains():
                      "thread_local mt19937(42) stream (u)")
 
 
+REF = os.environ.get("A11_REFERENCE", "/root/reference")
+
+
+def _reference_attention_statements():
+    """The decode-attention statements of the reference's forward_layer, as
+    source text read from its file (executed below, not copied here)."""
+    lines = open(os.path.join(REF, "engine", "pipeline.py")).read().splitlines()
+    i0 = next(i for i, l in enumerate(lines) if "Grouped Query Attention" in l)
+    i1 = next(i for i in range(i0, len(lines)) if lines[i].strip().startswith("attn_out ="))
+    block = lines[i0:i1 + 1]
+    indent = min(len(l) - len(l.lstrip()) for l in block if l.strip())
+    return "\n".join(l[indent:] for l in block)
+
+
+def attn_chains():
+    import math
+    import types
+    import torch
+    import torch.nn.functional as F
+    sys.path.insert(0, REF)
+    from engine.kv_cache import KVCacheManager  # the reference's paged KV cache
+    code = compile(_reference_attention_statements(), "engine/pipeline.py (decode attention)", "exec")
+    out = {}
+    for ci, (ctx, n, hkv, seed) in enumerate(((37, 6, 2, 11), (130, 4, 1, 12), (0, 5, 4, 13))):
+        hq, d = 8 * hkv, 128
+        g = torch.Generator().manual_seed(seed)
+        k = torch.randn(ctx + n, hkv, d, generator=g).to(torch.bfloat16)
+        v = torch.randn(ctx + n, hkv, d, generator=g).to(torch.bfloat16)
+        q = torch.randn(n, hq, d, generator=g).to(torch.bfloat16)
+        cache = KVCacheManager(n_layers=1, n_head_kv=hkv, head_dim=d, page_size=16)
+        if ctx:
+            cache.append(0, k[:ctx], v[:ctx])  # the prompt
+        res = []
+        for i in range(n):  # decode the chain token by token, as stream_inference does
+            cache.append(0, k[ctx + i:ctx + i + 1], v[ctx + i:ctx + i + 1])
+            k_cat, v_cat = cache.get_kv(0, 0, ctx + i + 1)
+            ns = dict(torch=torch, math=math, F=F, k_cat=k_cat, v_cat=v_cat, q=q[i:i + 1],
+                      cfg=types.SimpleNamespace(n_head=hq, n_head_kv=hkv, head_dim=d),
+                      self=types.SimpleNamespace(compute_dtype=torch.bfloat16))
+            exec(code, ns)
+            res.append(ns["attn_out"].reshape(hq, d))
+        bits = lambda t: t.contiguous().view(torch.int16).numpy()
+        out[f"c{ci}_meta"] = np.array([ctx, n, hkv], np.int32)
+        out[f"c{ci}_q"], out[f"c{ci}_k"], out[f"c{ci}_v"] = bits(q), bits(k), bits(v)
+        out[f"c{ci}_out"] = bits(torch.stack(res).to(torch.bfloat16))
+    return out
+
+
 if __name__ == "__main__":
     oracle.build()
     if not oracle.build_ref():
@@ -74,4 +130,5 @@ if __name__ == "__main__":
         json.dump(c1(), f, indent=1)
     with open(os.path.join(HERE, "ref_chains.json"), "w") as f:
         json.dump(ref_chains(), f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "attn_chains.npz"), **attn_chains())
     print("golden fixtures written")
