@@ -170,3 +170,69 @@ def test_decoder_steps_keep_pages_on_device(dev):
         used = set(pt[pt >= 0].cpu().tolist())
         assert used.isdisjoint(set(pool.free_pages().cpu().tolist())) and len(used) == int(want.sum())
         last = torch.stack([last[:, 1], res.bonus.clamp_min(0)], dim=1).contiguous()
+
+
+def test_matches_the_reference_manager_itself(dev):
+    """The device allocator against the reference's own PagedKVCacheManager
+    (src/cuda/paged_kv_cache.cu, built from the reference tree into
+    oracle/_ref/libref_kv.so with a C shim; it cudaMallocs its 256 blocks). The
+    same random batches go to both: a batch reserve is the reference's
+    allocate_sequence / append_token loop in batch order, a masked free its
+    free_sequence loop (a sequence of the batch without pages is started with
+    allocate_sequence, which takes its first block even for 0 tokens, as the
+    device reserve documents). Block tables must be identical after every batch."""
+    import ctypes
+    import os
+    path = os.path.join(os.path.dirname(oracle.__file__), "_ref", "libref_kv.so")
+    if not os.path.exists(path):
+        pytest.skip("oracle/_ref/libref_kv.so not built (needs the reference tree at build time)")
+    L = ctypes.CDLL(path)
+    L.ref_kv_create.restype = ctypes.c_void_p
+    L.ref_kv_create.argtypes = [ctypes.c_uint32]
+    L.ref_kv_destroy.argtypes = [ctypes.c_void_p]
+    for f in (L.ref_kv_allocate, L.ref_kv_free):
+        f.argtypes = [ctypes.c_void_p, ctypes.c_uint32]
+    L.ref_kv_append.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_uint32]
+    L.ref_kv_table.argtypes = [ctypes.c_void_p, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_int]
+    L.ref_kv_used_blocks.restype = ctypes.c_size_t
+    L.ref_kv_used_blocks.argtypes = [ctypes.c_void_p]
+    B, MP, P = 10, 40, 256
+    ref = L.ref_kv_create(B)
+    assert ref, "reference manager construction failed"
+    try:
+        pool = KVPagePool(P, dev)
+        pt = torch.full((B, MP), -1, dtype=torch.int32, device=dev)
+        sl = torch.zeros(B, dtype=torch.int32, device=dev)
+        active = np.zeros(B, bool)
+        lens = np.zeros(B, np.int64)
+        rng = np.random.default_rng(23)
+        buf = (ctypes.c_int32 * MP)()
+        for step in range(40):
+            if step % 5 == 4 and active.any():  # free a random set of active sequences
+                mask = active & (rng.random(B) < 0.5)
+                pool.free_sequences(pt, sl, torch.from_numpy(mask.astype(np.int32)).to(dev), check_status=True)
+                for b in np.nonzero(mask)[0]:
+                    assert L.ref_kv_free(ref, int(b)) == 0
+                active &= ~mask
+                lens[mask] = 0
+            else:  # every sequence adds 0..40 tokens, without running out of pages
+                add = rng.integers(0, 41, B)
+                add[(lens + add + 15) // 16 > MP] = 0
+                if int(np.maximum(1, (lens + add + 15) // 16).sum()) > P:
+                    continue
+                pool.reserve(pt, sl, torch.from_numpy(add.astype(np.int32)).to(dev), check_status=True)
+                for b in range(B):
+                    if not active[b]:
+                        assert L.ref_kv_allocate(ref, b) == 0
+                        active[b] = True
+                    if add[b]:
+                        assert L.ref_kv_append(ref, b, int(add[b])) == 0
+                lens += add
+            got = pt.cpu().numpy()
+            for b in range(B):
+                n = L.ref_kv_table(ref, b, buf, MP)
+                want = list(buf[:n]) if n >= 0 else []
+                assert got[b, :len(want)].tolist() == want and (got[b, len(want):] == -1).all(), (step, b)
+            assert P - int(pool.free_top.item()) == L.ref_kv_used_blocks(ref), step
+    finally:
+        L.ref_kv_destroy(ref)
