@@ -122,6 +122,43 @@ def attn_chains():
     return out
 
 
+def sampler_probs():
+    """Probabilities of the reference's TokenSampler (engine/sampler.py) with
+    top-k and top-p off, i.e. softmax(logits / max(T, 1e-5)): the sampler
+    runs unchanged, and the probabilities it hands to torch.multinomial are
+    recorded. Logits come from a seeded numpy generator the tests rerun."""
+    import torch
+    sys.path.insert(0, REF)
+    from engine.sampler import TokenSampler  # the reference's sampler
+    cases = []
+    for seed, vocab, temperature in ((21, 32000, 0.7), (22, 151936, 1.3), (23, 4096, 0.05)):
+        x = sampler_logits(seed, vocab)
+        seen = {}
+        multinomial = torch.multinomial
+        def record(probs, num_samples=1, **kw):
+            seen["p"] = probs.detach().clone()
+            return multinomial(probs, num_samples, **kw)
+        torch.multinomial = record
+        try:
+            TokenSampler(temperature=temperature, top_k=0, top_p=1.0).sample_next_token(torch.from_numpy(x.copy()))
+        finally:
+            torch.multinomial = multinomial
+        p = seen["p"].double().numpy()
+        rng = np.random.default_rng(seed + 100)
+        idx = [int(i) for i in np.argsort(-x)[:8]] + [int(i) for i in rng.choice(vocab, 55, replace=False)]
+        cases.append(dict(seed=seed, vocab=vocab, temperature=temperature, tokens=idx,
+                          probs=[float(p[i]) for i in idx]))
+    return dict(cases=cases, note="p(token) of engine/sampler.py TokenSampler(T, top_k=0, top_p=1.0); logits from "
+                                  "sampler_logits(seed, vocab) in make_golden.py")
+
+
+def sampler_logits(seed, vocab):
+    """The logits of a sampler_probs case (also rebuilt by the tests)."""
+    x = np.random.default_rng(seed).normal(0.0, 3.0, vocab).astype(np.float32)
+    x[seed % vocab] += 10.0
+    return x
+
+
 if __name__ == "__main__":
     oracle.build()
     if not oracle.build_ref():
@@ -131,4 +168,6 @@ if __name__ == "__main__":
     with open(os.path.join(HERE, "ref_chains.json"), "w") as f:
         json.dump(ref_chains(), f, indent=1)
     np.savez_compressed(os.path.join(HERE, "attn_chains.npz"), **attn_chains())
+    with open(os.path.join(HERE, "sampler_probs.json"), "w") as f:
+        json.dump(sampler_probs(), f, indent=1)
     print("golden fixtures written")
