@@ -9,26 +9,35 @@
 //
 // One CTA = one sequence b, one KV head g, 32 tree nodes x 8 query heads as
 // two Q tiles of 128 rows (the MMA M), one split of the KV range. 384 threads:
-//   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane
-//   warp 8     TMA producer: Q once, then K and V blocks of 128 keys (8 pages,
-//              one 64x16 box per page and 64-column half) into a 3-slot K
-//              ring and a 2-slot V ring shared by both tiles (a K slot frees
-//              after QK^T, long before PV); page ids fetched 4 blocks ahead
-//   warp 9     TMEM allocator + single-thread MMA issuer
-//   warps 10-11 idle (they complete the third warpgroup for the register split:
+//   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane;
+//              at the start each thread copies its Q row into TMEM
+//   warp 8     TMA producer: K and V blocks of 128 keys (8 pages, one 64x16
+//              box per page and 64-column half) into a 3-slot K ring and a
+//              2-slot V ring shared by both tiles; page ids fetched 4 blocks
+//              ahead
+//   warp 9     TMEM allocator + S issuer (QK^T groups)
+//   warp 11    PV issuer
+//   warp 10    idle (completes the third warpgroup for the register split:
 //              softmax warps 216 registers, warps 8-11 56)
-// TMEM (512 columns): per tile one S/P buffer of 128 columns and O (128 dims).
-// Per block j and tile: S_j = Q K_j^T (8 x tcgen05.mma M128 N128 K16), the
-// softmax warps mask it (ancestor bits), exponentiate (one packed FFMA per
-// pair of scores, one ex2 each), round P_j to bf16 (nearest even) and, with
-// fp32 row sums of the unrounded values, store it over the first 64
-// columns of the same buffer, then O += P_j V_j (8 MMAs M128 N128 K16, A = P
-// read from TMEM, V an MN-major shared-memory operand). S_{j+1} of a tile is
-// issued once PV_j of that tile has completed (S and P share columns); the
-// two tiles alternate, so one tile's softmax overlaps the other's MMAs.
+// TMEM (512 columns): one S buffer of 128 columns used by the tiles in turn,
+// O of each tile (128 dims), Q of each tile as bf16 pairs (64 columns).
+// Per block j and tile t: S = Q_t K_j^T (8 x tcgen05.mma M128 N128 K16, A = Q
+// from TMEM, K a K-major shared-memory operand). The softmax warps load S
+// into registers and release the buffer at once (the other tile's S is
+// computed into it meanwhile), mask it (ancestor bits), exponentiate (one
+// packed FFMA per pair of scores, one ex2 each), keep fp32 row sums of the
+// unrounded values and store P_t rounded to bf16 (nearest even) into shared
+// memory in the 128-byte-swizzled K-major layout; then O_t += P_t V_j (8 MMAs,
+// A = P from shared memory, V an MN-major shared-memory operand).
+// Two issuer threads: a thread's next shared-memory access (an mbarrier
+// poll) waits until the tensor core has read its MMAs' shared-memory
+// operands, so one thread issuing both kinds of group leaves the tensor pipe
+// idle between them; with S and PV on separate threads each polls and issues
+// while the other's group executes.
 // Why this shape: an M128 N64 K16 MMA costs about 58 cycles whatever its
-// operands, against 32 of math, while N = 128 runs at its math rate; and P in
-// TMEM keeps the tensor core's shared-memory port (about 128 B/clk) for Q, K, V.
+// operands, against 32 of math, while N = 128 runs at its math rate; P in
+// shared memory lets S(j+1) overwrite the S buffer while P(j) waits for PV,
+// instead of PV(j) having to finish first.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
 // exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
@@ -54,30 +63,30 @@ constexpr int kTiles = 2;             // Q tiles per CTA, 128 rows each
 constexpr int kNodesPerTile = 16;
 constexpr int kNodesPerCta = kTiles * kNodesPerTile;
 constexpr int kSoftmaxWarps = 4 * kTiles;
-constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1;
-constexpr int kTcThreads = 32 * (kSoftmaxWarps + 4);  // + producer, issuer, 2 idle: whole warpgroups
+constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kPvWarp = kSoftmaxWarps + 3;
+constexpr int kTcThreads = 32 * (kSoftmaxWarps + 4);  // + producer, 2 issuers, 1 idle: whole warpgroups
 constexpr int kRegsSoftmax = 216, kRegsOther = 56;    // setmaxnreg split (multiples of 8)
 constexpr long long kRegsNeeded = 32ll * (kSoftmaxWarps * kRegsSoftmax + 4 * kRegsOther);
-constexpr uint32_t kQHalf = 16384;    // Q tile: 128 rows x 128 B per 64-dim half
+constexpr uint32_t kPHalf = 16384;    // P tile: 128 rows x 128 B per 64-key half
 constexpr uint32_t kKVHalf = 16384;   // K or V: 128 tokens x 128 B per 64-dim half
-constexpr uint32_t kOffQ = 0;                                // tile t at 2*kQHalf*t
+constexpr uint32_t kOffP = 0;                                // P of tile t at 2*kPHalf*t
 constexpr uint32_t kSlotBytes = 2 * kKVHalf;                 // one K or V block: 32 KB
-constexpr uint32_t kOffK = kTiles * 2 * kQHalf;              // K slots
+constexpr uint32_t kOffK = kTiles * 2 * kPHalf;              // K slots
 constexpr uint32_t kOffV = kOffK + kKStages * kSlotBytes;    // V slots
 constexpr uint32_t kOffBar = kOffV + kVStages * kSlotBytes;  // 229376
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-constexpr uint32_t kTmemCols = 512;   // S/P[tile] at 128 t (P over its first 64 columns), O[tile] at 256 + 128 t
-constexpr uint32_t kColO = 256;
+// TMEM (512 columns): one S buffer shared by the tiles, O[tile], Q[tile] (bf16 pairs)
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColO = 128, kColQ = 384;
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, kBlockKV, false);
 constexpr uint32_t kIdescPV = tc::idesc_bf16_f32(128, 128, true);
 
 struct Bars {
-    uint64_t q_full;
     uint64_t k_full[kKStages], k_empty[kKStages], v_full[kVStages], v_empty[kVStages];
-    uint64_t s_full[kTiles], p_full[kTiles], p_free[kTiles];
-    uint64_t drain;
+    uint64_t q_ready, s_full[kTiles], s_free, p_full[kTiles], pv_done[kTiles];
+    uint64_t drain, drain_pv;
     uint32_t tmem_base;
     int32_t abort;
     uint64_t anc[kNodesPerCta];
@@ -86,6 +95,7 @@ static_assert(sizeof(Bars) <= 512, "barrier block");
 static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct TcParams {
+    const __nv_bfloat16 *q;
     const int32_t *page_table;
     int32_t max_pages, num_pages;
     const int32_t *ctx_lens, *parents, *n_nodes;
@@ -138,8 +148,7 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
 }
 
 __global__ void __launch_bounds__(kTcThreads, 1)
-    tree_attn_tc(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                 const __grid_constant__ CUtensorMap tv, const TcParams p) {
+    tree_attn_tc(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars *bs = reinterpret_cast<Bars *>(sm + kOffBar);
@@ -183,7 +192,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
     // ---------------- setup ----------------
     if (tid == 0) {
-        tc::mbar_init(&bs->q_full, 1);
         for (int s = 0; s < kKStages; ++s) {
             tc::mbar_init(&bs->k_full[s], 1);
             tc::mbar_init(&bs->k_empty[s], 1);
@@ -194,10 +202,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         }
         for (int t = 0; t < kTiles; ++t) {
             tc::mbar_init(&bs->s_full[t], 1);
-            tc::mbar_init(&bs->p_full[t], 128);
-            tc::mbar_init(&bs->p_free[t], 1);
+            tc::mbar_init(&bs->p_full[t], 4);  // one arrival per softmax warp of the tile
+            tc::mbar_init(&bs->pv_done[t], 1);
         }
+        tc::mbar_init(&bs->s_free, 4);
+        tc::mbar_init(&bs->q_ready, kSoftmaxWarps);
         tc::mbar_init(&bs->drain, 1);
+        tc::mbar_init(&bs->drain_pv, 1);
         bs->abort = 0;
         tc::fence_barrier_init();
     }
@@ -241,7 +252,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncthreads();
     tc::tc_fence_after();
     const uint32_t tmem = bs->tmem_base;
-
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     // Register split per warpgroup (setmaxnreg acts on whole warpgroups):
     // warps 8-11 give registers back, the softmax warps take them. The total
     // stays within the launch's registers (checked on the host before launch).
@@ -251,16 +262,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         if (warp == kProducerWarp) {
             // ---------------- TMA producer ----------------
             if (lane == 0) {
-                tc::prefetch_tmap(&tq);
                 tc::prefetch_tmap(&tk);
                 tc::prefetch_tmap(&tv);
-                tc::mbar_arrive_expect_tx(&bs->q_full, kTiles * 2 * kQHalf);
-                for (int t = 0; t < kTiles; ++t) {
-                    const int qrow = b * p.N + node0 + t * kNodesPerTile;
-                    uint8_t *sQ = sm + kOffQ + t * 2 * kQHalf;
-                    tc::tma_load_3d(sQ, &tq, &bs->q_full, 0, g * 8, qrow);
-                    tc::tma_load_3d(sQ + kQHalf, &tq, &bs->q_full, 64, g * 8, qrow);
-                }
             }
             // Page ids of 4 blocks (32 entries) per coalesced warp load, double
             // buffered, so a block's ids were requested 4 blocks before use.
@@ -316,85 +319,120 @@ __global__ void __launch_bounds__(kTcThreads, 1)
             }
             if (aborted(bs) && lane == 0) {
                 // drain copies that may still be landing in this CTA's shared memory
-                tc::mbar_wait(&bs->q_full, 0, kWaitBudget);
                 for (int i = max(0, nk - kKStages); i < nk; ++i)
                     tc::mbar_wait(&bs->k_full[i % kKStages], (i / kKStages) & 1, kWaitBudget);
                 for (int i = max(0, nv - kVStages); i < nv; ++i)
                     tc::mbar_wait(&bs->v_full[i % kVStages], (i / kVStages) & 1, kWaitBudget);
             }
         } else if (warp == kMmaWarp) {
-            // ---------------- MMA issuer ----------------
+            // ---------------- S issuer ----------------
             if (lane == 0) {
-                auto issue_s = [&](int it, int t) {  // S(it) of tile t: 8 MMAs M128 N128 K16
-                    const uint32_t k_addr = tc::smem_u32(sm + kOffK + (it % kKStages) * kSlotBytes);
-                    const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
+                auto issue_s = [&](int j, int t) {  // S = Q_t K_j^T: 8 MMAs M128 N128 K16, A = Q from TMEM
+                    const uint32_t k_addr = tc::smem_u32(sm + kOffK + (j % kKStages) * kSlotBytes);
     #pragma unroll
-                    for (int kk = 0; kk < 8; ++kk) {
-                        const uint32_t qoff = (kk >> 2) * kQHalf + (kk & 3) * 32;
-                        const uint32_t koff = (kk >> 2) * kKVHalf + (kk & 3) * 32;
-                        tc::mma_bf16_ss(tmem + t * 128, tc::sdesc_sw128(q_addr + qoff, 16, 1024),
-                                        tc::sdesc_sw128(k_addr + koff, 16, 1024), kIdescS, kk > 0);
-                    }
+                    for (int kk = 0; kk < 8; ++kk)
+                        tc::mma_bf16_ts(tmem + kColS, tmem + kColQ + 64 * t + kk * 8,
+                                        tc::sdesc_sw128(k_addr + (kk >> 2) * kKVHalf + (kk & 3) * 32, 16, 1024),
+                                        kIdescS, kk > 0);
                     tc::mma_commit(&bs->s_full[t]);
-                    if (t == kTiles - 1) tc::mma_commit(&bs->k_empty[it % kKStages]);
+                    if (t == kTiles - 1) tc::mma_commit(&bs->k_empty[j % kKStages]);
                 };
-                bool ok = wait_or_abort(&bs->q_full, 0, bs, p.status);
-                ok = ok && wait_or_abort(&bs->k_full[0], 0, bs, p.status);
-                if (ok) {
+                // S groups in the order u = 2 j + t: S(u) needs the S buffer
+                // (the tile before has loaded S(u - 1)) and K(j). Every phase
+                // waited for is the next one of its barrier.
+                bool ok = wait_or_abort(&bs->q_ready, 0, bs, p.status);
+                for (int u = 0; u < kTiles * nb && ok; ++u) {
+                    const int j = u / kTiles, t = u % kTiles;
+                    if (u > 0) ok = wait_or_abort(&bs->s_free, (u - 1) & 1, bs, p.status);
+                    if (ok && t == 0) ok = wait_or_abort(&bs->k_full[j % kKStages], (j / kKStages) & 1, bs, p.status);
+                    if (!ok) break;
                     tc::tc_fence_after();
-                    for (int t = 0; t < kTiles; ++t) issue_s(0, t);
-                }
-                // Per block and tile: PV(it) once the tile's P is in TMEM, then
-                // S(it + 1) once PV(it) has read P (S and P share the columns).
-                // The other tile's softmax runs meanwhile, so the tensor pipe
-                // alternates between the tiles.
-                for (int it = 0; it < nb && ok && !aborted(bs); ++it) {
-                    const int vs = it % kVStages;
-                    const uint32_t v_addr = tc::smem_u32(sm + kOffV + vs * kSlotBytes);
-                    for (int t = 0; t < kTiles && ok; ++t) {
-                        if (!wait_or_abort(&bs->p_full[t], it & 1, bs, p.status)) { ok = false; break; }
-                        if (t == 0 && !wait_or_abort(&bs->v_full[vs], (it / kVStages) & 1, bs, p.status)) { ok = false; break; }
-                        tc::tc_fence_after();
-    #pragma unroll
-                        for (int kk = 0; kk < kBlockKV / 16; ++kk) {
-                            tc::mma_bf16_ts(tmem + kColO + t * 128, tmem + t * 128 + kk * 8,
-                                            tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
-                                            (it > 0 || kk > 0) ? 1u : 0u);
-                        }
-                        tc::mma_commit(&bs->p_free[t]);
-                        if (t == kTiles - 1) tc::mma_commit(&bs->v_empty[vs]);
-                        if (it + 1 < nb) {
-                            if (t == 0 && !wait_or_abort(&bs->k_full[(it + 1) % kKStages], ((it + 1) / kKStages) & 1, bs,
-                                                         p.status)) { ok = false; break; }
-                            if (!wait_or_abort(&bs->p_free[t], it & 1, bs, p.status)) { ok = false; break; }
-                            tc::tc_fence_after();
-                            issue_s(it + 1, t);
-                        }
-                    }
+                    issue_s(j, t);
                 }
                 // wait for every issued MMA before the CTA may release TMEM
                 tc::mma_commit(&bs->drain);
                 tc::mbar_wait(&bs->drain, 0, kWaitBudget);
             }
             __syncwarp();
+        } else if (warp == kPvWarp) {
+            // ---------------- PV issuer ----------------
+            if (lane == 0) {
+                auto issue_pv = [&](int j, int t) {  // O_t += P_t V_j: 8 MMAs M128 N128 K16, A = P from shared memory
+                    const uint32_t v_addr = tc::smem_u32(sm + kOffV + (j % kVStages) * kSlotBytes);
+                    const uint32_t p_addr = tc::smem_u32(sm + kOffP + t * 2 * kPHalf);
+    #pragma unroll
+                    for (int kk = 0; kk < kBlockKV / 16; ++kk)
+                        tc::mma_bf16_ss(tmem + kColO + 128 * t,
+                                        tc::sdesc_sw128(p_addr + (kk >> 2) * kPHalf + (kk & 3) * 32, 16, 1024),
+                                        tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
+                                        (j > 0 || kk > 0) ? 1u : 0u);
+                    tc::mma_commit(&bs->pv_done[t]);
+                    if (t == kTiles - 1) tc::mma_commit(&bs->v_empty[j % kVStages]);
+                };
+                // PV groups in the same order: P_t(j) stored and V(j) landed.
+                bool ok = true;
+                for (int u = 0; u < kTiles * nb && ok; ++u) {
+                    const int j = u / kTiles, t = u % kTiles;
+                    ok = wait_or_abort(&bs->p_full[t], j & 1, bs, p.status);
+                    if (ok && t == 0) ok = wait_or_abort(&bs->v_full[j % kVStages], (j / kVStages) & 1, bs, p.status);
+                    if (!ok) break;
+                    tc::tc_fence_after();
+                    issue_pv(j, t);
+                }
+                tc::mma_commit(&bs->drain_pv);
+                tc::mbar_wait(&bs->drain_pv, 0, kWaitBudget);
+            }
+            __syncwarp();
         }
     } else {
         asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(kRegsSoftmax));
         // ---------------- softmax warps: tile = warp / 4, thread = query row ----------------
+        // Q row of this thread into TMEM as the A operand of QK^T (bf16 pairs,
+        // lane = row): 256 bytes, zeros past the last node. The issuer
+        // waits for q_ready before the first S.
+        {
+            uint32_t qv[64];
+            if (node < p.N) {
+                const uint4 *src = reinterpret_cast<const uint4 *>(p.q + (((size_t)b * p.N + node) * p.Hq + row_head) * 128);
+#pragma unroll
+                for (int c = 0; c < 16; ++c) {
+                    const uint4 v = __ldg(src + c);
+                    qv[4 * c] = v.x;
+                    qv[4 * c + 1] = v.y;
+                    qv[4 * c + 2] = v.z;
+                    qv[4 * c + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int c = 0; c < 64; ++c) qv[c] = 0u;
+            }
+            tc::tmem_st32u(tmem + lane_base + kColQ + 64 * tile, qv);
+            tc::tmem_st32u(tmem + lane_base + kColQ + 64 * tile + 32, qv + 32);
+            tc::tmem_wait_st();
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bs->q_ready);
+        }
+        // `ok` stays warp-uniform for the .sync.aligned TMEM accesses.
         const bool live = node < n_live;
         const uint64_t anc = bs->anc[node - node0];
-        const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-        const uint32_t col_s = tile * 128, col_o = kColO + tile * 128;
+        // this row of P_t; XOR-ing 16-byte slot numbers into it gives the 128-byte swizzle
+        const uint32_t p_row = (tc::smem_u32(sm + kOffP + tile * 2 * kPHalf + m * 128)) ^ (uint32_t)((m & 7) << 4);
         const float sl2 = p.scale_log2;
         float m_ref = -INFINITY, lsum = 0.0f;
         bool ok = true;
         for (int it = 0; it < nb && ok; ++it) {
             const int p0 = (blk0 + it) * kBlockKV;
-            if (!wait_or_abort(&bs->s_full[tile], it & 1, bs, p.status)) { ok = false; break; }
+            ok = __all_sync(0xffffffffu, wait_or_abort(&bs->s_full[tile], it & 1, bs, p.status));
+            if (!ok) break;
             tc::tc_fence_after();
             float xa[64], xb[64];  // keys 0-63 and 64-127 of the block
-            tc::tmem_ld64(tmem + lane_base + col_s, xa);
-            tc::tmem_ld64(tmem + lane_base + col_s + 64, xb);
+            tc::tmem_ld64(tmem + lane_base + kColS, xa);
+            tc::tmem_ld64(tmem + lane_base + kColS + 64, xb);
+            // S is in registers: the other tile's S may overwrite the buffer
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bs->s_free);
 #define X(c) ((c) < 64 ? xa[(c) & 63] : xb[(c) & 63])
             // mask (raw scores) and block max
             if (live && p0 + kBlockKV > L) {
@@ -430,43 +468,50 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 }
             }
             const float neg = m_ref == -INFINITY ? 0.0f : -m_ref;
-            float2 ls[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
-            // P as bf16 pairs (lower key in the low half) over the first 64
-            // columns of the S buffer, in four stores of 32 keys (S is in
-            // registers, so overwriting its columns is safe), one wait at the end.
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-                uint32_t pw[16];
-#pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const float2 e = tc::ffma2(make_float2(X(32 * h + 2 * c), X(32 * h + 2 * c + 1)),
-                                               make_float2(sl2, sl2), make_float2(neg, neg));
-                    const float2 a = make_float2(tc::ex2(e.x), tc::ex2(e.y));
-                    pw[c] = tc::cvt_bf16x2(a.x, a.y);
-                    ls[c & 3] = tc::fadd2(ls[c & 3], a);  // fp32 denominator of the unrounded p
-                }
-                tc::tmem_st16u_nowait(tmem + lane_base + col_s + 16 * h, pw);
+            // PV(it - 1) of this tile must have completed: it read P_t from
+            // shared memory (about to be overwritten) and accumulated into O.
+            if (it > 0) {
+                ok = __all_sync(0xffffffffu, wait_or_abort(&bs->pv_done[tile], (it - 1) & 1, bs, p.status));
+                if (!ok) break;
+                tc::tc_fence_after();
             }
-            tc::tmem_wait_st();
+            float2 ls[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
+            // P as bf16 pairs (lower key in the low half), 16 bytes per 8 keys:
+            // chunk c of the row goes to 16-byte slot c ^ (row & 7) of its
+            // 64-key half (the 128-byte swizzle of a K-major operand).
+#pragma unroll
+            for (int c8 = 0; c8 < kBlockKV / 8; ++c8) {
+                uint32_t pw[4];
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float2 ev = tc::ffma2(make_float2(X(8 * c8 + 2 * e), X(8 * c8 + 2 * e + 1)),
+                                                make_float2(sl2, sl2), make_float2(neg, neg));
+                    const float2 a = make_float2(tc::ex2(ev.x), tc::ex2(ev.y));
+                    pw[e] = tc::cvt_bf16x2(a.x, a.y);
+                    ls[e] = tc::fadd2(ls[e], a);  // fp32 denominator of the unrounded p
+                }
+                tc::st_shared_v4((p_row + (uint32_t)(c8 >> 3) * kPHalf) ^ (uint32_t)((c8 & 7) << 4), pw);
+            }
             lsum = lsum * alpha + (((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y)));
-            // Rescale O (after the scores are dead, before PV(it) may start):
-            // PV(it-1) has completed, since S(it) was computed after it.
+            // Rescale O before PV(it) may start (the scores are dead by now).
             if (__any_sync(0xffffffffu, rescale) && it > 0) {
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + 128 * tile + c * 32, o);
 #pragma unroll
                     for (int e = 0; e < 32; ++e) o[e] *= alpha;
-                    tc::tmem_st32(tmem + lane_base + col_o + c * 32, o);
+                    tc::tmem_st32(tmem + lane_base + kColO + 128 * tile + c * 32, o);
                 }
             }
+            tc::fence_proxy_async_smem();  // P visible to the tensor core
             tc::tc_fence_before();
-            tc::mbar_arrive(&bs->p_full[tile]);
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(&bs->p_full[tile]);
 #undef X
         }
         // ---------------- epilogue ----------------
-        if (ok && wait_or_abort(&bs->p_free[tile], (nb - 1) & 1, bs, p.status)) {
+        if (ok && __all_sync(0xffffffffu, wait_or_abort(&bs->pv_done[tile], (nb - 1) & 1, bs, p.status))) {
             tc::tc_fence_after();
             const size_t row = ((size_t)b * p.N + node) * p.Hq + row_head;
             const bool write = node < p.N;
@@ -476,7 +521,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + 128 * tile + c * 32, o);
                     if (write) {
 #pragma unroll
                         for (int q = 0; q < 4; ++q) {
@@ -499,7 +544,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     float o[32];
-                    tc::tmem_ld32(tmem + lane_base + col_o + c * 32, o);
+                    tc::tmem_ld32(tmem + lane_base + kColO + 128 * tile + c * 32, o);
                     if (write)
 #pragma unroll
                         for (int q = 0; q < 8; ++q)
@@ -600,13 +645,7 @@ bool encode(CUtensorMap *map, const void *base, int rank, const cuuint64_t *dims
 }  // namespace
 
 cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
-    CUtensorMap tq, tk, tv;
-    {  // Q [B*N rows][Hq][128]: box 64 dims x 8 heads x 16 nodes
-        const cuuint64_t dims[3] = {128, (cuuint64_t)a.Hq, (cuuint64_t)a.B * a.N};
-        const cuuint64_t str[2] = {256, (cuuint64_t)a.Hq * 256};
-        const cuuint32_t box[3] = {64, 8, kNodesPerTile};
-        if (!encode(&tq, a.q, 3, dims, str, box)) return cudaErrorInvalidValue;
-    }
+    CUtensorMap tk, tv;
     {  // K, V [pages][16][Hkv][128]: box 64 dims x 1 head x 16 tokens x 1 page
         const cuuint64_t dims[4] = {128, (cuuint64_t)a.Hkv, 16, (cuuint64_t)a.num_pages};
         const cuuint64_t str[3] = {256, (cuuint64_t)a.Hkv * 256, (cuuint64_t)a.Hkv * 256 * 16};
@@ -623,6 +662,7 @@ cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
         if ((long long)fa.numRegs * kTcThreads < kRegsNeeded) return cudaErrorInvalidConfiguration;
     }
     TcParams p{};
+    p.q = reinterpret_cast<const __nv_bfloat16 *>(a.q);
     p.page_table = a.page_table;
     p.max_pages = a.max_pages;
     p.num_pages = a.num_pages;
@@ -641,7 +681,7 @@ cudaError_t launch_tree_attention(const AttnArgs &a, cudaStream_t s) {
     p.part_ml = a.part_ml;
     p.status = a.status;
     const dim3 grid((a.N + kNodesPerCta - 1) / kNodesPerCta, a.Hkv * a.splits, a.B);
-    tree_attn_tc<<<grid, kTcThreads, kSmemBytes, s>>>(tq, tk, tv, p);
+    tree_attn_tc<<<grid, kTcThreads, kSmemBytes, s>>>(tk, tv, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess || a.splits == 1) return e;
     const size_t rows = (size_t)a.B * a.N * a.Hq;
