@@ -121,7 +121,9 @@ int tree_attention_splits(int32_t B, int32_t N, int32_t Hq, int32_t Hkv, int32_t
         const int bps = (blocks + s - 1) / s;
         if (s > 1 && bps < 8) break;
         const long long waves = (ctas * s + sms - 1) / sms;
-        const double cost = (double)waves * (bps + 4.0);  // ~4 blocks of fixed per-CTA cost
+        // ~12 blocks of fixed cost per CTA: Q into TMEM, filling the K/V rings
+        // and the S chain, the epilogue (fitted to a forced-split sweep)
+        const double cost = (double)waves * (bps + 12.0);
         if (cost < best_cost * 0.98) { best_cost = cost; best = s; }
     }
     return best;
