@@ -176,11 +176,13 @@ def run_ours(args, rank, world, local_rank):
     grown = torch.empty(B, dtype=torch.int32, device=dev)
     ev_attn = []
 
-    def step(timed_events=None, inputs=None, ready=None):
+    def step(timed_events=None, inputs=None, ready=None, out_free=None):
         # inputs: (hidden, q, last, uniforms) of this step; default the resident
         # set with uniforms drawn on the device. ready: events of the copies of
         # (last, q, hidden, uniforms); each input is waited for just before its
         # first use, so a step starts while its later inputs are still copying.
+        # out_free: event after which the acceptance outputs may be rewritten
+        # (the previous step's device-to-host copy of them has completed).
         hid, qq, lst, un = (hidden, q, last, None) if inputs is None else inputs
 
         def wait(j):
@@ -207,6 +209,8 @@ def run_ours(args, rank, world, local_rank):
         if un is None:
             uni.uniform_(generator=gen)
             un = uni
+        if out_free is not None:
+            torch.cuda.current_stream().wait_event(out_free)
         a11spec.accept(a11spec.STOCH_ONEHOT, logits.view(B, MAX_NODES, VOCAB), tk, pa, nn,
                        temperature=TEMP, uniforms=un, stats=stats, out=acc)
         a11spec.kv_compact(k_pool, v_pool, page_table, ctx_lens, acc.accept_len, acc.accepted_nodes,
@@ -271,17 +275,27 @@ def run_ours(args, rank, world, local_rank):
                 d_.copy_(h_, non_blocking=True)
                 ready[k % 2][j].record(copy_stream)
 
+    # The results go to the host on a stream of their own, so the next step's
+    # kernels do not queue behind the copies; its acceptance waits for them.
+    d2h_stream = torch.cuda.Stream(device=dev)
+    step_done, out_free = torch.cuda.Event(), torch.cuda.Event()
+
     def e2e_run(n):
         copy_stream.wait_stream(torch.cuda.current_stream())  # copies start after the timing event
         h2d(0)
         for k in range(n):
             if k + 1 < n:
                 h2d(k + 1)
-            step(inputs=ins[k % 2], ready=ready[k % 2])
+            step(inputs=ins[k % 2], ready=ready[k % 2], out_free=out_free if k > 0 else None)
             free[k % 2].record()
-            h_out_tok.copy_(acc.accepted_tokens, non_blocking=True)
-            h_out_len.copy_(acc.accept_len, non_blocking=True)
-            h_out_bonus.copy_(acc.bonus, non_blocking=True)
+            step_done.record()
+            with torch.cuda.stream(d2h_stream):
+                d2h_stream.wait_event(step_done)
+                h_out_tok.copy_(acc.accepted_tokens, non_blocking=True)
+                h_out_len.copy_(acc.accept_len, non_blocking=True)
+                h_out_bonus.copy_(acc.bonus, non_blocking=True)
+                out_free.record(d2h_stream)
+        torch.cuda.current_stream().wait_stream(d2h_stream)  # the last results are inside the timed region
 
     e2e_run(max(1, args.warmup // 2))
     barrier()
