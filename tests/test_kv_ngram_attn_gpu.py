@@ -174,3 +174,24 @@ def test_tree_attention_c4_shape_sampled(dev):
         got = out[b:b + 1].float().cpu().numpy()
         err = np.abs(got - ref).max() / np.abs(ref).max()
         assert err < 2e-2, (b, err)
+
+
+def test_tree_attention_c5_shape_one_kv_head(dev):
+    """C5 shapes (B=32, ctx 32768, 64 nodes, GQA 32/4): the launch runs
+    unsplit, 257 blocks of 128 keys per CTA. One sequence's first KV head (its
+    8 query heads) is checked against the oracle, which keeps the CPU side to
+    a few seconds."""
+    d = W.make_c4(seed=5, batch=32, ctx=32768, pool_pages=32 * 2053 + 64, device=dev)
+    out, _, _ = a11spec.tree_attention(d["q"], d["k_pool"], d["v_pool"], d["page_table"], d["ctx_lens"],
+                                       d["parents"], d["n_nodes"], check_status=True)
+    b = 7
+    pages = d["page_table"][b].long()  # this sequence's pages, gathered into a pool of their own
+    ref, _, rc = oracle.tree_attention(
+        d["q"][b:b + 1, :, 0:8].float().cpu().numpy(), d["k_pool"][pages, :, 0:1].float().cpu().numpy(),
+        d["v_pool"][pages, :, 0:1].float().cpu().numpy(),
+        np.arange(len(pages), dtype=np.int32)[None, :], d["ctx_lens"][b:b + 1].cpu().numpy(),
+        d["parents"][b:b + 1].cpu().numpy(), d["n_nodes"][b:b + 1].cpu().numpy(), 1 / np.sqrt(128))
+    assert rc == 0
+    got = out[b:b + 1, :, 0:8].float().cpu().numpy()
+    err = np.abs(got - ref).max() / np.abs(ref).max()
+    assert err < 2e-2, err
