@@ -25,6 +25,9 @@ constexpr int kNgramWarps = 4;
 static_assert(kNgramWarps * 3 * A11S_MAX_NODES * sizeof(int32_t) <= 48 * 1024,
               "the per-warp trees fit the default dynamic shared memory");
 
+// kSlots: a compile-time bound on a.slots, so the bucket and the selection
+// state stay in registers (every slot index is a constant after unrolling).
+template <int kSlots>
 __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const NgramArgs a) {
     extern __shared__ int32_t ng_tree[];  // per warp: tokens, parents, depths [max_nodes] each
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -44,32 +47,32 @@ __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const Ng
         const int w = depth == 0 ? a.width_root : a.width_inner;
         for (int g = lvl_start; g < lvl_end && n < M; g += 32) {
             const int i = g + lane;
-            int sel_tok[32];
+            int32_t st[kSlots], sc[kSlots];
+#pragma unroll
+            for (int s2 = 0; s2 < kSlots; ++s2) sc[s2] = 0;  // slots past a.slots count as empty
             int cnt = 0;
             if (i < lvl_end) {
                 const int32_t t = stk[i];
                 const int32_t prev = i == 0 ? prev0 : stk[spa[i]];
                 const int32_t *bk = a.table + (size_t)bucket_of(prev, t, a.log2_buckets) * a.slots * 2;
-                int32_t st[32], sc[32];
                 if (vec) {
-                    for (int s2 = 0; s2 < a.slots; s2 += 2) {
-                        const int4 v = __ldg(reinterpret_cast<const int4 *>(bk + 2 * s2));
-                        st[s2] = v.x; sc[s2] = v.y; st[s2 + 1] = v.z; sc[s2 + 1] = v.w;
+#pragma unroll
+                    for (int s2 = 0; s2 < kSlots; s2 += 2) {
+                        if (s2 < a.slots) {
+                            const int4 v = __ldg(reinterpret_cast<const int4 *>(bk + 2 * s2));
+                            st[s2] = v.x; sc[s2] = v.y;
+                            if (s2 + 1 < kSlots) { st[s2 + 1] = v.z; sc[s2 + 1] = v.w; }
+                        }
                     }
                 } else {
-                    for (int s2 = 0; s2 < a.slots; ++s2) { st[s2] = __ldg(bk + 2 * s2); sc[s2] = __ldg(bk + 2 * s2 + 1); }
+#pragma unroll
+                    for (int s2 = 0; s2 < kSlots; ++s2)
+                        if (s2 < a.slots) { st[s2] = __ldg(bk + 2 * s2); sc[s2] = __ldg(bk + 2 * s2 + 1); }
                 }
-                unsigned used = 0;
-                for (int r = 0; r < w; ++r) {
-                    int best = -1;
-                    for (int s2 = 0; s2 < a.slots; ++s2) {
-                        if (((used >> s2) & 1u) || sc[s2] <= 0) continue;
-                        if (best < 0 || sc[s2] > sc[best]) best = s2;
-                    }
-                    if (best < 0) break;
-                    used |= 1u << best;
-                    sel_tok[cnt++] = st[best];
-                }
+                // how many continuations: up to w slots with a positive count
+#pragma unroll
+                for (int s2 = 0; s2 < kSlots; ++s2) cnt += sc[s2] > 0 ? 1 : 0;
+                cnt = min(cnt, w);
             }
             // exclusive prefix of child counts across the lanes of this group
             int incl = cnt;
@@ -79,9 +82,18 @@ __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const Ng
                 if (lane >= o) incl += y;
             }
             const int base = n + incl - cnt;
+            // children in rank order: highest count first, lower slot among equals
+            unsigned used = 0;
             for (int r = 0; r < cnt; ++r) {
+                int best = -1, bc = 0, bt = 0;
+#pragma unroll
+                for (int s2 = 0; s2 < kSlots; ++s2) {
+                    const bool take = !((used >> s2) & 1u) && sc[s2] > 0 && (best < 0 || sc[s2] > bc);
+                    if (take) { best = s2; bc = sc[s2]; bt = st[s2]; }
+                }
+                used |= 1u << best;
                 const int idx = base + r;
-                if (idx < M) { stk[idx] = sel_tok[r]; spa[idx] = i; sde[idx] = depth + 1; }
+                if (idx < M) { stk[idx] = bt; spa[idx] = i; sde[idx] = depth + 1; }
             }
             n = min(M, n + __shfl_sync(0xffffffffu, incl, 31));
             __syncwarp();
@@ -104,7 +116,11 @@ __global__ void __launch_bounds__(kNgramWarps * 32) ngram_expand_kernel(const Ng
 
 cudaError_t launch_ngram_expand(const NgramArgs &a, cudaStream_t s) {
     const size_t smem = (size_t)kNgramWarps * 3 * a.max_nodes * sizeof(int32_t);  // <= 48 KB for max_nodes <= 1024
-    ngram_expand_kernel<<<(a.B + kNgramWarps - 1) / kNgramWarps, kNgramWarps * 32, smem, s>>>(a);
+    const unsigned grid = (a.B + kNgramWarps - 1) / kNgramWarps;
+    if (a.slots <= 4) ngram_expand_kernel<4><<<grid, kNgramWarps * 32, smem, s>>>(a);
+    else if (a.slots <= 8) ngram_expand_kernel<8><<<grid, kNgramWarps * 32, smem, s>>>(a);
+    else if (a.slots <= 16) ngram_expand_kernel<16><<<grid, kNgramWarps * 32, smem, s>>>(a);
+    else ngram_expand_kernel<32><<<grid, kNgramWarps * 32, smem, s>>>(a);
     return cudaGetLastError();
 }
 
