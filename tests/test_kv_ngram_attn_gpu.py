@@ -28,6 +28,22 @@ def test_ngram_expand_vs_oracle(dev, widths):
         np.testing.assert_array_equal(got.cpu().numpy(), o[key], err_msg=key)
 
 
+
+@pytest.mark.parametrize("slots", [1, 3, 4, 5, 16, 27, 32])
+def test_ngram_expand_slot_counts(dev, slots):
+    """Every compiled slot bound (4, 8, 16, 32), odd counts (the 4-byte bucket
+    reads) and ties of count across a whole bucket, against the oracle."""
+    rng = np.random.default_rng(10 + slots)
+    table = W.make_ngram_table(log2_buckets=10, slots=slots, vocab=3000, seed=slots)
+    table[..., 1][rng.random(table.shape[:2]) < 0.25] = 0
+    table[3, :, 1] = 2
+    last = rng.integers(0, 3000, (19, 2)).astype(np.int32)
+    wr, wi = min(slots, 4), min(slots, 3)
+    g = a11spec.ngram_expand(torch.from_numpy(table).to(dev), torch.from_numpy(last).to(dev), wr, wi, 4, 64)
+    o = oracle.ngram_expand(table, 10, last, wr, wi, 4, 64)
+    for got, key in zip(g, ("tokens", "parents", "depths", "n_nodes")):
+        np.testing.assert_array_equal(got.cpu().numpy(), o[key], err_msg=key)
+
 def test_ngram_bucket_host_device_agree():
     for a, b in [(0, 0), (3, 4), (151935, 12), (-7, 2**31 - 1)]:
         assert a11spec.ngram_bucket(a, b, 20) == oracle.ngram_bucket(a, b, 20)
