@@ -105,3 +105,17 @@ def test_shard_partition(gb, world):
     assert spans[0][0] == 0 and spans[-1][1] == gb
     assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
     assert max(s[1] - s[0] for s in spans) - min(s[1] - s[0] for s in spans) <= 1
+
+
+def test_attention_split_planner_picks():
+    """The split planner (waves x (blocks per split + 12)) as seen through the
+    workspace size, on the 148-SM count it assumes without a device: the C5
+    and C4 batches run unsplit (header only), one long sequence splits 18 ways
+    and eight split 2 ways (partials of B x N x Hq x (D + 2) floats per split)."""
+    import a11spec
+    f = a11spec.ops.tree_attention_workspace_bytes
+    per_split = lambda B: B * 64 * 32 * (128 + 2) * 4
+    assert f(32, 64, 32, 4, 128, 32768 + 128) == 256
+    assert f(16, 64, 32, 4, 128, 4096 + 64) == 256
+    assert f(1, 64, 32, 4, 128, 32832) == 256 + 18 * per_split(1)
+    assert f(8, 64, 32, 4, 128, 32832) == 256 + 2 * per_split(8)
