@@ -11,7 +11,6 @@
 // until the process exits. Nothing here calls cudaMalloc, cudaFree or an
 // allocating library routine.
 #include <cstdio>
-#include <mutex>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -19,9 +18,22 @@
 static __device__ __align__(256) unsigned char g_accept_scratch[A11S_ACCEPT_STATIC_SCRATCH_BYTES];
 
 namespace {
-constexpr int kMaxDevices = 64;
-std::mutex g_scratch_mutex;
-void *g_scratch_ptr[kMaxDevices];  // device address of g_accept_scratch, per device
+// Largest batch whose a11s_accept_workspace_bytes() fits the array (0 if none).
+int32_t largest_fitting_batch(int32_t mode, int32_t max_nodes, int32_t vocab) {
+    int32_t lo = 0, hi = 1;
+    while (hi < (1 << 30) && a11s_accept_workspace_bytes(mode, hi, max_nodes, vocab) <= A11S_ACCEPT_STATIC_SCRATCH_BYTES) {
+        lo = hi;
+        hi *= 2;
+    }
+    while (hi - lo > 1) {  // invariant: lo fits, hi does not
+        const int32_t mid = lo + (hi - lo) / 2;
+        if (a11s_accept_workspace_bytes(mode, mid, max_nodes, vocab) <= A11S_ACCEPT_STATIC_SCRATCH_BYTES)
+            lo = mid;
+        else
+            hi = mid;
+    }
+    return lo;
+}
 }  // namespace
 
 extern "C" int a11s_accept_static(int32_t mode, int32_t dtype, const void *target_logits,
@@ -34,39 +46,35 @@ extern "C" int a11s_accept_static(int32_t mode, int32_t dtype, const void *targe
                                   int32_t *status, void *stream) {
     const size_t need = a11s_accept_workspace_bytes(mode, batch, max_nodes, vocab);
     if (need > A11S_ACCEPT_STATIC_SCRATCH_BYTES) {
-        char msg[256];
+        char msg[320];
         snprintf(msg, sizeof msg,
-                 "a11s_accept_static: needs %zu scratch bytes but the fixed array holds %u "
-                 "(8 bytes per row chunk: batch * max_nodes * ceil(vocab / 2048) of them); call a11s_accept "
-                 "with a workspace instead",
-                 need, (unsigned)A11S_ACCEPT_STATIC_SCRATCH_BYTES);
+                 "a11s_accept_static: this call needs %zu scratch bytes but the fixed array holds %u; "
+                 "at max_nodes %d and vocab %d in mode %d at most %d sequences fit per call. Split the "
+                 "batch, or call a11s_accept with a workspace",
+                 need, (unsigned)A11S_ACCEPT_STATIC_SCRATCH_BYTES, max_nodes, vocab, mode,
+                 largest_fitting_batch(mode, max_nodes, vocab));
         return a11s::set_error(A11S_ENOSPACE, msg);
     }
-    // Per-device set-up on the first call with that device current: the host
-    // name g_accept_scratch is only a stand-in, its device address comes from
-    // cudaGetSymbolAddress.
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices)
-        return a11s::set_error(A11S_ECUDA, "a11s_accept_static: no usable current device");
+    // The host name g_accept_scratch is only a stand-in; the array's device
+    // address comes from cudaGetSymbolAddress, asked on every call for the
+    // context current now. Caching it per device ordinal would go stale after a
+    // cudaDeviceReset or under another context on the same device. The lookup
+    // allocates nothing; the first one on a device may load the module, so make
+    // the first call before any stream capture.
     void *scratch = nullptr;
-    {
-        std::lock_guard<std::mutex> lock(g_scratch_mutex);
-        if (!g_scratch_ptr[dev]) {
-            void *p = nullptr;
-            if (cudaGetSymbolAddress(&p, g_accept_scratch) != cudaSuccess || !p)
-                return a11s::set_error(A11S_ECUDA, "a11s_accept_static: cudaGetSymbolAddress failed");
-            g_scratch_ptr[dev] = p;
-        }
-        scratch = g_scratch_ptr[dev];
+    if (cudaGetSymbolAddress(&scratch, g_accept_scratch) != cudaSuccess || !scratch) {
+        (void)cudaGetLastError();
+        return a11s::set_error(A11S_ECUDA, "a11s_accept_static: cudaGetSymbolAddress failed");
     }
     // a11s_accept clears the status word and the row counters (the only parts
     // that must start at zero; every record is written before it is read) on
-    // the stream before its kernel runs.
+    // the stream before its kernel runs; with batch == 0 it clears the status
+    // word alone, which is then copied out like any other.
     const int rc = a11s_accept(mode, dtype, target_logits, draft_logits, row_stride, temperature,
                                uniforms, tokens, parents, n_nodes, batch, max_nodes, vocab,
                                accept_len, accepted_nodes, accepted_tokens, bonus, node_probs,
                                stats, scratch, A11S_ACCEPT_STATIC_SCRATCH_BYTES, stream);
-    if (rc != A11S_OK || !status || batch == 0) return rc;
+    if (rc != A11S_OK || !status) return rc;
     const cudaError_t e = cudaMemcpyAsync(status, scratch, 2 * sizeof(int32_t), cudaMemcpyDeviceToDevice,
                                           reinterpret_cast<cudaStream_t>(stream));
     return e == cudaSuccess ? A11S_OK : a11s::set_error(A11S_ECUDA, "a11s_accept_static: status copy failed");

@@ -9,16 +9,28 @@ sampling acceptance at T=0.7 with seeded uniforms, and KV compaction. Inputs are
 seeded synthetic tensors (no dataset exists for this path).
 
 metric: accepted tokens/s (emitted tokens = accepted drafts + bonus, summed over
-all ranks, over the max-over-ranks device time).
+all ranks, over the max-over-ranks device time). On one GPU the line also
+carries `configs`: device time per launch and roofline fraction of the kernels
+of the four single-GPU configurations (greedy chain, greedy tree, sampling
+against draft logits, tree attention + greedy acceptance + compaction).
 
 Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-Multi-GPU: launched by torch.distributed.run, one rank per GPU, NCCL only for
-the per-step acceptance counters.
+Multi-GPU: launched by torch.distributed.run, one rank per GPU. The only
+collective is an all-reduce of the acceptance counters every few steps, on a
+side stream, so it overlaps the compute stream.
+
+--impl reference times the same per-GPU step on the host cores the reference's
+way (its attention statements, LM head and sampler in torch, its own C++
+verifier for the acceptance decisions where oracle/_ref is built). That arm
+never loads liba11spec.so: it reads the seeded generators from
+a11spec/workloads.py by file path, without importing the package.
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -27,7 +39,8 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path[:0] = [ROOT, os.path.join(ROOT, "a11-llm-optimizer_b200")]
+PKG = os.path.join(ROOT, "a11-llm-optimizer_b200")
+sys.path[:0] = [ROOT, PKG]
 
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
@@ -38,6 +51,9 @@ B_PER_GPU, CTX, MAX_NODES, HQ, HKV, D, HIDDEN, VOCAB, TEMP = 32, 32768, 64, 32, 
 WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH = 4, 2, 5
 SPARE_PAGES = 32  # per sequence: room for the context to grow by the committed tokens
 LOG2_BUCKETS = 20
+REDUCE_EVERY = 5  # steps between two all-reduces of the acceptance counters (multi-GPU)
+STAT_NAMES = ("steps_accepted", "steps_rejected", "fallback_count", "total_draft_tokens",
+              "total_steps", "emitted_tokens")
 
 
 def peaks():
@@ -64,6 +80,26 @@ def profile_traffic(kernel_key: str):
                 except ValueError:
                     return None
     return None
+
+
+def workloads_module():
+    """a11spec/workloads.py loaded by file path: it needs numpy and torch only,
+    so the host arms never load the CUDA library through the package."""
+    spec = importlib.util.spec_from_file_location("a11spec_workloads_host",
+                                                  os.path.join(PKG, "a11spec", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def workload_config(world: int) -> dict:
+    """The `config` of both arms' lines (the driver compares them)."""
+    return {"workload": "C5 end-to-end draft->reserve pages->verify->accept->compact->release pages, "
+                        "32 seqs/GPU, context growing from 32768 by the committed tokens",
+            "seqs_per_gpu": B_PER_GPU, "global_seqs": B_PER_GPU * world, "ctx": CTX, "max_nodes": MAX_NODES,
+            "gqa": f"{HQ}/{HKV}", "head_dim": D, "vocab": VOCAB, "temperature": TEMP,
+            "parallelism": f"request-batch dp{world}",
+            "l2": "inputs larger than L2 (2.15 GB KV + 622 MB logits per step)"}
 
 
 def gpu_id(dev) -> str:
@@ -134,6 +170,117 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
+def device_time_us(fn, iters: int, pre=None) -> float:
+    """Mean device time of fn(i) over `iters` launches, each between its own
+    pair of CUDA events on the current stream. A GPU-side spin queued first
+    keeps the device busy while the host enqueues every launch, so host launch
+    overhead never shows up as device time. pre(i) runs outside the events."""
+    torch.cuda.synchronize()
+    torch.cuda._sleep(100_000_000)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
+    for i, (a, b) in enumerate(evs):
+        if pre is not None:
+            pre(i)
+        a.record()
+        fn(i)
+        b.record()
+    torch.cuda.synchronize()
+    return 1e3 * sum(a.elapsed_time(b) for a, b in evs) / iters
+
+
+# ----------------------------------------------------------------------------- C1-C4 kernels
+def measure_configs(dev, pk) -> dict:
+    """Device time per launch of the kernels of the single-GPU configurations,
+    with algorithmic bytes or FLOPs and the fraction of the measured peak.
+    Between timed launches the inputs rotate over copies larger than L2 in
+    total (C1, C2), or a single copy already exceeds L2 (C3, C4)."""
+    import a11spec
+    from a11spec import workloads as W
+
+    hbm = pk["hbm"]
+    out = {}
+
+    def hbm_entry(us, nbytes, launches, note):
+        gbs = nbytes / (us * 1e-6) / 1e9
+        return {"us_per_launch": us, "bytes_per_launch": nbytes, "achieved_gbs": gbs,
+                "frac_hbm": gbs / hbm, "kernel_launches": launches, "note": note}
+
+    # C1: greedy chain, B=1, fp32 [6, 32000]: latency-bound
+    d = W.make_c1(seed=1)
+    copies = 200  # 200 x 768 KB = 154 MB > L2
+    lg = torch.from_numpy(d["logits"]).to(dev).expand(copies, -1, -1, -1).contiguous()
+    tk, pa, nn = (torch.from_numpy(d[k]).to(dev) for k in ("tokens", "parents", "n_nodes"))
+    acc = a11spec.ops.alloc_accept(a11spec.GREEDY, 1, 6, 32000, dev)
+    us = device_time_us(lambda i: a11spec.accept(a11spec.GREEDY, lg[i], tk, pa, nn, out=acc), copies)
+    out["C1_greedy_chain"] = {"us_per_launch": us, "bytes_per_launch": 6 * 32000 * 4, "bound": "latency",
+                              "kernel_launches": 2, "accept_len": int(acc.accept_len[0]),
+                              "note": "record init + accept kernel; inputs rotate over 200 copies (154 MB)"}
+    del lg
+
+    # C2: greedy complete binary tree, B=8, bf16 [8, 31, 151936], 60 % forced matches
+    d = W.make_c2(seed=2)
+    copies = 3  # 3 x 75 MB > L2
+    lg = d["logits_bf16"].to(dev).expand(copies, -1, -1, -1).contiguous()
+    tk, pa, nn = (torch.from_numpy(d[k]).to(dev) for k in ("tokens", "parents", "n_nodes"))
+    acc = a11spec.ops.alloc_accept(a11spec.GREEDY, 8, 31, VOCAB, dev)
+    us = device_time_us(lambda i: a11spec.accept(a11spec.GREEDY, lg[i % copies], tk, pa, nn, out=acc), 30)
+    e = hbm_entry(us, 8 * 31 * VOCAB * 2, 2, "record init + accept kernel; inputs rotate over 3 copies (226 MB)")
+    e["mean_accept_len"] = float(acc.accept_len.float().mean())
+    out["C2_greedy_tree"] = e
+    del lg
+
+    # C3: sampling against draft logits, T=0.8, B=64, 63 drafts, fp32 p and q (4.98 GB)
+    d = W.make_c3(seed=3, device=dev)
+    acc = a11spec.ops.alloc_accept(a11spec.STOCH_DRAFT, 64, 64, VOCAB, dev)
+    us = device_time_us(lambda i: a11spec.accept(a11spec.STOCH_DRAFT, d["p"], d["tokens"], d["parents"], d["n_nodes"],
+                                                 draft_logits=d["q"], temperature=0.8, uniforms=d["uniforms"],
+                                                 out=acc), 4)
+    e = hbm_entry(us, 2 * 64 * 64 * VOCAB * 4, 2, "record init + accept kernel; p and q read once")
+    e["mean_accept_len"] = float(acc.accept_len.float().mean())
+    out["C3_draft_sampling"] = e
+    del d, acc
+
+    # C4: tree attention (ctx 4096, GQA 32/4, 64-node random trees) + greedy accept + compaction, B=32
+    d = W.make_c4(seed=4, device=dev)
+    B, N = 32, 64
+    attn_out = torch.empty_like(d["q"])
+    ws = a11spec.ops.workspace(a11spec.ops.tree_attention_workspace_bytes(B, N, HQ, HKV, D, 4096 + N), dev)
+    us = device_time_us(lambda i: a11spec.tree_attention(d["q"], d["k_pool"], d["v_pool"], d["page_table"],
+                                                         d["ctx_lens"], d["parents"], d["n_nodes"], out=attn_out,
+                                                         ws=ws), 10)
+    flops = 4.0 * B * HQ * N * (4096 + N / 2) * D
+    tf = flops / (us * 1e-6) / 1e12
+    out["C4_tree_attention"] = {"us_per_launch": us, "flops_per_launch": flops, "achieved_tflops": tf,
+                                "frac_tensor_burst": tf / pk["tflops"], "bound": "tensor",
+                                "note": "KV 273 MB + Q/O 34 MB per launch"}
+    acc = a11spec.ops.alloc_accept(a11spec.GREEDY, B, N, VOCAB, dev)
+    us = device_time_us(lambda i: a11spec.accept(a11spec.GREEDY, d["logits"], d["tokens"], d["parents"],
+                                                 d["n_nodes"], out=acc), 10)
+    e = hbm_entry(us, B * N * VOCAB * 2, 2, "record init + accept kernel; 622 MB of logits")
+    e["mean_accept_len"] = float(acc.accept_len.float().mean())
+    out["C4_greedy_accept"] = e
+    pt0, len0 = d["page_table"].clone(), d["ctx_lens"].clone()
+    freed = torch.full_like(pt0, -1)
+    n_freed = torch.zeros(B, dtype=torch.int32, device=dev)
+    kws = a11spec.ops.workspace(256, dev)
+
+    def restore(i):
+        d["page_table"].copy_(pt0)
+        d["ctx_lens"].copy_(len0)
+
+    us = device_time_us(lambda i: a11spec.kv_compact(d["k_pool"], d["v_pool"], d["page_table"], d["ctx_lens"],
+                                                     acc.accept_len, acc.accepted_nodes, d["n_nodes"],
+                                                     freed_pages=freed, n_freed=n_freed, ws=kws), 10, pre=restore)
+    moved = int(acc.accept_len.sum())
+    out["C4_compaction"] = {"us_per_launch": us, "bytes_per_launch": 2 * 2 * moved * HKV * D * 2,
+                            "bound": "latency", "kernel_launches": 2, "rows_moved": moved,
+                            "note": "K and V rows of the accepted nodes read and written once, then the "
+                                    "page-table shrink"}
+    del d, acc
+    torch.cuda.empty_cache()
+    return out
+
+
 # ----------------------------------------------------------------------------- our arm
 def run_ours(args, rank, world, local_rank):
     import a11spec
@@ -145,6 +292,9 @@ def run_ours(args, rank, world, local_rank):
     st = W.make_c5(seed=5 + 1000 * rank, batch=B, ctx=CTX, max_nodes=MAX_NODES, num_q_heads=HQ,
                    num_kv_heads=HKV, head_dim=D, hidden=HIDDEN, vocab=VOCAB, log2_buckets=LOG2_BUCKETS,
                    device=str(dev), temperature=TEMP, spare_pages=SPARE_PAGES)
+    host_copy = None
+    if world == 1 and not args.no_cpu_baseline:
+        host_copy = host_state(st)  # before the step changes the page tables and lengths
     table, q, hidden, w = st["table"], st["q"], st["hidden"], st["w"]
     k_pool, v_pool = st["k_pool"], st["v_pool"]
     page_table, ctx_lens = st["page_table"], st["ctx_lens"]
@@ -174,7 +324,36 @@ def run_ours(args, rank, world, local_rank):
     n_freed = torch.zeros(B, dtype=torch.int32, device=dev)
     kv_ws = a11spec.ops.workspace(256, dev)
     grown = torch.empty(B, dtype=torch.int32, device=dev)
-    ev_attn = []
+    ev_kernels = []  # per timed step: (attention start, end, accept start, end)
+
+    # Acceptance counters: K3 accumulates them on the device every step. Every
+    # REDUCE_EVERY steps a snapshot is all-reduced over the ranks on a side
+    # stream, so the collective overlaps the next steps' kernels instead of
+    # sitting on the compute stream; two snapshot buffers alternate, and a
+    # buffer is rewritten only after the all-reduce that last read it.
+    side = torch.cuda.Stream(device=dev) if world > 1 else None
+    snaps = [torch.zeros_like(stats) for _ in range(2)]
+    snap_read = [torch.cuda.Event(), torch.cuda.Event()]
+    snap_taken = torch.cuda.Event()
+    reduce_state = {"steps": 0, "reduces": 0, "last": None}
+
+    def reduce_counters():
+        k = reduce_state["steps"]
+        reduce_state["steps"] += 1
+        if side is None or k % REDUCE_EVERY != REDUCE_EVERY - 1:
+            return
+        j = reduce_state["reduces"] % 2
+        cur = torch.cuda.current_stream()
+        if reduce_state["reduces"] >= 2:
+            cur.wait_event(snap_read[j])
+        snaps[j].copy_(stats)
+        snap_taken.record(cur)
+        side.wait_event(snap_taken)
+        with torch.cuda.stream(side):
+            torch.distributed.all_reduce(snaps[j], op=torch.distributed.ReduceOp.SUM)
+            snap_read[j].record(side)
+        reduce_state["reduces"] += 1
+        reduce_state["last"] = (j, reduce_state["steps"])
 
     def step(timed_events=None, inputs=None, ready=None, out_free=None):
         # inputs: (hidden, q, last, uniforms) of this step; default the resident
@@ -193,16 +372,15 @@ def run_ours(args, rank, world, local_rank):
         tk, pa, de, nn = a11spec.ngram_expand(table, lst, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES, out=tree)
         grown.copy_(ctx_lens)
         pages.reserve(page_table, grown, nn)  # pages for the tree slots ctx_lens + i
+        evs = None
         if timed_events is not None:
-            e0 = torch.cuda.Event(enable_timing=True)
-            e1 = torch.cuda.Event(enable_timing=True)
-            e0.record()
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            evs[0].record()
         wait(1)
         a11spec.tree_attention(qq, k_pool, v_pool, page_table, ctx_lens, pa, nn, max_kv_len=max_kv,
                                out=attn_out, ws=attn_ws)
-        if timed_events is not None:
-            e1.record()
-            timed_events.append((e0, e1))
+        if evs:
+            evs[1].record()
         wait(2)
         torch.matmul(hid, w, out=logits)
         wait(3)
@@ -211,15 +389,19 @@ def run_ours(args, rank, world, local_rank):
             un = uni
         if out_free is not None:
             torch.cuda.current_stream().wait_event(out_free)
+        if evs:
+            evs[2].record()
         a11spec.accept(a11spec.STOCH_ONEHOT, logits.view(B, MAX_NODES, VOCAB), tk, pa, nn,
                        temperature=TEMP, uniforms=un, stats=stats, out=acc)
+        if evs:
+            evs[3].record()
+            timed_events.append(evs)
         a11spec.kv_compact(k_pool, v_pool, page_table, ctx_lens, acc.accept_len, acc.accepted_nodes,
                            nn, freed_pages=freed, n_freed=n_freed, ws=kv_ws)
         pages.release(freed, n_freed)
         # next root pair: (last accepted token or old root, bonus)
         a11spec.next_roots(tk, acc.accepted_tokens, acc.accept_len, acc.bonus, lst)
-        if world > 1:
-            torch.distributed.all_reduce(stats.clone(), op=torch.distributed.ReduceOp.SUM)
+        reduce_counters()
 
     def barrier():
         if world > 1:
@@ -235,12 +417,13 @@ def run_ours(args, rank, world, local_rank):
         barrier()
         e_start.record()
         for _ in range(args.steps):
-            step(ev_attn)
+            step(ev_kernels)
         e_end.record()
         barrier()
     ms = e_start.elapsed_time(e_end)
-    emitted = int((stats - s0)[a11spec.STAT_NAMES.index("emitted_tokens")])
-    attn_ms = sum(a.elapsed_time(b) for a, b in ev_attn) / len(ev_attn)
+    emitted = int((stats - s0)[STAT_NAMES.index("emitted_tokens")])
+    attn_ms = sum(e[0].elapsed_time(e[1]) for e in ev_kernels) / len(ev_kernels)
+    acc_ms = sum(e[2].elapsed_time(e[3]) for e in ev_kernels) / len(ev_kernels)
 
     # end to end through the public API with host buffers: pinned H2D of the
     # step's inputs (hidden states, queries, uniforms, last tokens) and D2H of
@@ -309,152 +492,246 @@ def run_ours(args, rank, world, local_rank):
         barrier()
     clk.lines.extend(clk_e2e.lines)
     e2e_ms = x0.elapsed_time(x1)
-    e2e_emitted = int((stats - s1)[a11spec.STAT_NAMES.index("emitted_tokens")])
+    e2e_emitted = int((stats - s1)[STAT_NAMES.index("emitted_tokens")])
 
-    t = torch.tensor([ms, e2e_ms, attn_ms], dtype=torch.float64, device=dev)
+    if side is not None:
+        torch.cuda.current_stream().wait_stream(side)
+        torch.cuda.synchronize()
+    t = torch.tensor([ms, e2e_ms, attn_ms, acc_ms], dtype=torch.float64, device=dev)
     cnt = torch.tensor([emitted, e2e_emitted], dtype=torch.int64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(cnt, op=torch.distributed.ReduceOp.SUM)
-    ms, e2e_ms, attn_ms = (float(x) for x in t.tolist())
+    ms, e2e_ms, attn_ms, acc_ms = (float(x) for x in t.tolist())
     emitted, e2e_emitted = (int(x) for x in cnt.tolist())
     if rank != 0:
         return None
     pk = peaks()
     attn_flops = 4.0 * B * HQ * MAX_NODES * (CTX + MAX_NODES / 2) * D  # per launch, tree half-masked
     attn_tflops = attn_flops / (attn_ms * 1e-3) / 1e12
-    traffic = profile_traffic("tree_attention_c5")
+    acc_bytes = B * MAX_NODES * VOCAB * 2
+    acc_gbs = acc_bytes / (acc_ms * 1e-3) / 1e9
     line = {
         "metric": METRIC, "value": emitted / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded; no dataset exists for this path)",
-        "config": {"workload": "C5 end-to-end draft->reserve pages->verify->accept->compact->release pages, "
-                               "32 seqs/GPU, context growing from 32768 by the committed tokens",
-                   "seqs_per_gpu": B, "global_seqs": B * world, "ctx": CTX, "max_nodes": MAX_NODES,
-                   "gqa": f"{HQ}/{HKV}", "head_dim": D, "vocab": VOCAB, "temperature": TEMP,
-                   "parallelism": f"request-batch dp{world}",
-                   "l2": "inputs larger than L2 (2.15 GB KV + 622 MB logits per step)"},
+        "config": workload_config(world),
         "mean_emitted_per_seq": emitted / (args.steps * B * world),
-        "kernel_us": {"tree_attention": attn_ms * 1e3},
+        "kernel_us": {"tree_attention": attn_ms * 1e3, "accept": acc_ms * 1e3},
+        # the timed region is tens of milliseconds, so the burst GEMM peak is the denominator
         "roofline": {"kernel": "tree_attention", "bound": "tensor", "achieved": attn_tflops,
-                     "peak": pk["tflops_sus"], "unit": "TFLOP/s", "frac": attn_tflops / pk["tflops_sus"],
-                     "peak_source": f"{pk['src']} bf16 sustained", "traffic": traffic,
-                     "flops_per_launch": attn_flops},
+                     "peak": pk["tflops"], "unit": "TFLOP/s", "frac": attn_tflops / pk["tflops"],
+                     "peak_source": f"{pk['src']} bf16 burst", "frac_of_sustained": attn_tflops / pk["tflops_sus"],
+                     "traffic": profile_traffic("tree_attention_c5"), "flops_per_launch": attn_flops},
+        "roofline_accept": {"kernel": "accept (one-hot sampling, T=0.7)", "bound": "hbm", "achieved": acc_gbs,
+                            "peak": pk["hbm"], "unit": "GB/s", "frac": acc_gbs / pk["hbm"],
+                            "peak_source": f"{pk['src']} HBM copy", "bytes_per_launch": acc_bytes,
+                            "us_includes": "record init + accept kernel"},
         "e2e": {"value": e2e_emitted / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo},
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }
-    if world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(st, args)
+    if reduce_state["last"] is not None:
+        j, through = reduce_state["last"]
+        line["acceptance_stats_global"] = dict(zip(STAT_NAMES, (int(x) for x in snaps[j].tolist())),
+                                               through_step=through, ranks=world)
+    if world == 1 and not args.no_configs:
+        line["configs"] = measure_configs(dev, pk)
+    if host_copy is not None:
+        line["cpu_baseline"] = cpu_baseline(host_copy)
     return line
 
 
-# ----------------------------------------------------------------------------- CPU paths
-def cpu_path_one_sequence(st, b, use_ref_verifier):
-    """The whole path for sequence b on the host: trigram expansion (oracle),
-    tree attention in torch exactly as engine/pipeline.py:391-402 computes it,
-    LM head, softmax, acceptance (reference verifier on the chain decisions
-    where it is built, else the oracle), compaction (oracle). Returns emitted
-    tokens."""
-    import oracle
-    table = st["table_np"]
-    last = st["last_np"][b:b + 1]
-    tr = oracle.ngram_expand(table, st["log2_buckets"], last, WIDTH_ROOT, WIDTH_INNER, MAX_DEPTH, MAX_NODES)
-    n = int(tr["n_nodes"][0])
-    par = tr["parents"][0]
-    # attention: gather this sequence's KV (fp32) and compute per node
-    pt = st["page_table_np"][b]
-    L = CTX
-    pos = np.arange(L + n)
-    pages = torch.from_numpy(pt[pos // 16].astype(np.int64))
-    slots = torch.from_numpy(pos % 16)
-    kk = st["k_pool"][pages, slots].float()  # [S, Hkv, D]
-    vv = st["v_pool"][pages, slots].float()
-    rep = HQ // HKV
-    kk = kk.repeat_interleave(rep, dim=1)
-    vv = vv.repeat_interleave(rep, dim=1)
-    q = st["q"][b, :n].float()  # [n, Hq, D]
-    scores = torch.einsum("nhd,shd->nhs", q, kk) / np.sqrt(D)
-    mask = torch.zeros(n, L + n, dtype=torch.bool)
-    for i in range(n):
-        a = i
-        while a >= 0:
-            mask[i, L + a] = True
-            a = int(par[a]) if a > 0 else -1
-    mask[:, :L] = True
-    scores.masked_fill_(~mask[:, None, :], float("-inf"))
-    probs = torch.softmax(scores, dim=-1).to(torch.bfloat16).float()
-    _ = torch.einsum("nhs,shd->nhd", probs, vv)
-    logits = st["hidden"][b * MAX_NODES: b * MAX_NODES + n].float() @ st["w"]
-    uni = np.random.default_rng(b).random((1, MAX_NODES), dtype=np.float32)
-    tgt = np.zeros((1, MAX_NODES, VOCAB), np.float32)
-    tgt[0, :n] = logits.numpy()
-    r = oracle.accept(1, tgt, tr["tokens"], tr["parents"], tr["n_nodes"], temperature=TEMP, uniforms=uni)
-    if use_ref_verifier and oracle.ref() is not None:
-        # the reference verifier judges the first-child chain on the same probabilities
-        chain = [1]
-        while True:
-            kids = [c for c in range(chain[-1] + 1, n) if par[c] == chain[-1]]
-            if not kids:
-                break
-            chain.append(kids[0])
-        probs_chain = r["node_probs"][0, chain].astype(np.float32)
-        oracle.ref_verify(tr["tokens"][0, chain], np.ones(len(chain), np.float32), probs_chain)
-    return int(r["accept_len"][0]) + 1
-
-
+# ----------------------------------------------------------------------------- host path
 def host_state(st):
-    return dict(table_np=st["table"].cpu().numpy(), log2_buckets=st["log2_buckets"],
-                last_np=st["last_tokens"].cpu().numpy(), page_table_np=st["page_table"].cpu().numpy(),
-                k_pool=st["k_pool"].cpu(), v_pool=st["v_pool"].cpu(), q=st["q"].cpu(),
-                hidden=st["hidden"].cpu(), w=st["w"].cpu().float())
+    return {k: (v.cpu() if torch.is_tensor(v) else v) for k, v in st.items()}
 
 
-def cpu_baseline(st, args):
-    hs = host_state(st)
+class HostStep:
+    """The per-GPU C5 step on the host cores, the reference's way where it has
+    one:
+    * draft trees: the oracle's restatement of the hashed trigram expansion (the
+      reference's draft is a formula over the last two tokens,
+      engine/speculative.py:13-24, with no table);
+    * attention: the decode-attention statements of engine/pipeline.py:391-402
+      (query head h reads KV head h // (Hq/Hkv) as repeat_interleave groups them,
+      fp32 scores scaled by 1/sqrt(d), softmax, probabilities cast to bf16, PV),
+      with the ancestor mask over the tree slots;
+    * LM head: hidden x W in fp32 (engine/pipeline.py:471);
+    * acceptance: p = softmax(logits / T) (engine/sampler.py:16, 37) of each
+      sequence's first-child chain, judged with deterministic drafts (q = 1) by the
+      reference's own verifier (src/engine/speculative_verifier.cpp:84-135,
+      compiled into oracle/_ref) with its thread_local mt19937(42) uniforms; the
+      oracle's restatement of that rule when oracle/_ref is absent. The bonus is
+      drawn from the last accepted node's row by torch.multinomial
+      (engine/sampler.py:37-38);
+    * the accepted K/V rows move to the contiguous slots after the context, which
+      grows by the committed tokens, and the next root pair is taken.
+    """
+
+    def __init__(self, st):
+        import oracle
+        self.oracle = oracle
+        self.ref = oracle.ref()
+        self.table = st["table"].numpy()
+        self.log2_buckets = st["log2_buckets"]
+        self.last = st["last_tokens"].numpy().copy()
+        self.k_pool, self.v_pool = st["k_pool"], st["v_pool"]
+        self.q = st["q"]
+        self.hidden = st["hidden"]
+        self.w32 = st["w"].float()
+        pt = st["page_table"].clone()
+        # the spare logical pages get the pool's unowned pages, in order
+        owned = pt[pt >= 0]
+        free = torch.ones(self.k_pool.shape[0], dtype=torch.bool)
+        free[owned.long()] = False
+        spare = torch.nonzero(free).flatten().int()
+        holes = pt < 0
+        pt[holes] = spare[: int(holes.sum())]
+        self.page_table = pt
+        self.ctx = st["ctx_lens"].numpy().astype(np.int64).copy()
+        self.gen = torch.Generator().manual_seed(77)
+        self.scale = 1.0 / math.sqrt(D)
+
+    @property
+    def kind(self) -> str:
+        return "reference" if self.ref is not None else "port"
+
+    def _attention(self, b, n, parents):
+        L = int(self.ctx[b])
+        pos = torch.arange(L + n)
+        pages = self.page_table[b, pos // 16].long()
+        k = self.k_pool[pages, pos % 16].float()  # [S, Hkv, D]
+        v = self.v_pool[pages, pos % 16].float()
+        q = self.q[b, :n].float()  # [n, Hq, D]
+        allowed = torch.zeros(n, L + n, dtype=torch.bool)
+        allowed[:, :L] = True
+        for i in range(n):
+            a = i
+            while a >= 0:
+                allowed[i, L + a] = True
+                a = int(parents[a]) if a > 0 else -1
+        rep = HQ // HKV
+        out = torch.empty(n, HQ, D)
+        for h in range(HKV):
+            qh = q[:, h * rep:(h + 1) * rep].reshape(n * rep, D)
+            s = (qh @ k[:, h].T).mul_(self.scale).view(n, rep, L + n)
+            s.masked_fill_(~allowed[:, None, :], float("-inf"))
+            p = torch.softmax(s, dim=-1).to(torch.bfloat16).float().view(n * rep, L + n)
+            out[:, h * rep:(h + 1) * rep] = (p @ v[:, h]).view(n, rep, D)
+        return out.to(torch.bfloat16)
+
+    def step(self, seqs) -> int:
+        """One step for the sequences `seqs`; returns their emitted tokens."""
+        o = self.oracle
+        seqs = list(seqs)
+        tr = o.ngram_expand(self.table, self.log2_buckets, self.last[seqs], WIDTH_ROOT, WIDTH_INNER,
+                            MAX_DEPTH, MAX_NODES)
+        rows, chains = [], []
+        for s, b in enumerate(seqs):
+            n = int(tr["n_nodes"][s])
+            par = tr["parents"][s]
+            self._attention(b, n, par)
+            rows.append(torch.arange(b * MAX_NODES, b * MAX_NODES + n))
+            chain = [0]  # the first-child chain from the root
+            while True:
+                kids = [c for c in range(chain[-1] + 1, n) if par[c] == chain[-1]]
+                if not kids:
+                    break
+                chain.append(kids[0])
+            chains.append(chain)
+        logits = self.hidden[torch.cat(rows)].float() @ self.w32  # [sum n, V]
+        offs = np.concatenate([[0], np.cumsum([len(r) for r in rows])])
+        K = max(1, max(len(c) - 1 for c in chains))
+        tok = np.zeros((len(seqs), K), np.int32)
+        drf = np.ones((len(seqs), K), np.float32)
+        tgt = np.zeros((len(seqs), K), np.float32)  # padding is rejected (p = 0)
+        for s, chain in enumerate(chains):
+            for i in range(1, len(chain)):
+                row = logits[offs[s] + chain[i - 1]]
+                x = int(tr["tokens"][s, chain[i]])
+                tok[s, i - 1] = x
+                tgt[s, i - 1] = float(torch.softmax(row / TEMP, dim=-1)[x])
+        if self.ref is not None:
+            alen = np.zeros(len(seqs), np.uint32)
+            self.ref.ref_verify_batch(len(seqs), K, tok, drf, tgt, alen, max(1, torch.get_num_threads()))
+            alen = alen.astype(np.int64)
+        else:
+            alen = o.verify_chain(drf, tgt, np.random.default_rng(42).random(tgt.shape, dtype=np.float32))[0]
+        emitted = 0
+        for s, b in enumerate(seqs):
+            chain, a = chains[s], int(min(alen[s], len(chains[s]) - 1))
+            probs = torch.softmax(logits[offs[s] + chain[a]] / TEMP, dim=-1)
+            bonus = int(torch.multinomial(probs, 1, generator=self.gen))
+            L = int(self.ctx[b])
+            for j in range(a):  # accepted node chain[j+1] moves from slot L + node to L + 1 + j
+                src, dst = L + chain[j + 1], L + 1 + j
+                ps, pd = self.page_table[b, src // 16].long(), self.page_table[b, dst // 16].long()
+                self.k_pool[pd, dst % 16] = self.k_pool[ps, src % 16]
+                self.v_pool[pd, dst % 16] = self.v_pool[ps, src % 16]
+            self.ctx[b] = L + 1 + a
+            newest = int(tr["tokens"][s, chain[a]])  # last accepted token, or the old root
+            self.last[b] = (newest, bonus)
+            emitted += a + 1
+        return emitted
+
+
+def cpu_baseline(hs) -> dict:
+    """The host path on a bounded sample of the per-GPU step (rank 0, one GPU)."""
+    path = HostStep(hs)
     threads = torch.get_num_threads()
+    path.step([B_PER_GPU - 1])  # warm-up (thread pools, first-touch pages)
+    sample = list(range(8))
     t0 = time.perf_counter()
-    emitted = cpu_path_one_sequence(hs, 0, use_ref_verifier=False)
+    emitted = path.step(sample)
     dt = time.perf_counter() - t0
-    return {"value": emitted / dt, "unit": UNIT, "cores": threads, "kind": "port",
-            "sample": f"1 of {B_PER_GPU} sequences of the per-GPU workload (whole path: trigram "
-                      f"expansion, tree attention over ctx {CTX}, LM head, sampling acceptance), "
-                      f"{dt:.1f} s; torch CPU ops for attention/LM head on {threads} threads, C oracle "
-                      f"for the rest"}
+    return {"value": emitted / dt, "unit": UNIT, "cores": threads, "kind": path.kind,
+            "sample": f"{len(sample)} of the {B_PER_GPU} sequences of one per-GPU step after a one-sequence "
+                      f"warm-up, {dt:.1f} s: trigram expansion (oracle), tree attention over ctx {CTX} and the "
+                      f"LM head in torch on {threads} threads, acceptance by the "
+                      f"{'reference verifier' if path.kind == 'reference' else 'oracle restatement'}"}
+
+
+HOST_SAMPLE = 8  # sequences of the per-GPU step that one host step processes
 
 
 def run_reference(args, rank, world):
-    """CPU path of the reference (its attention math engine/pipeline.py:391-402 in
-    torch, its verifier src/engine/speculative_verifier.cpp for the chain decisions)
-    with the oracle port for the parts the reference lacks."""
+    """The per-GPU step on the host cores (HostStep), on the arm's metric and
+    config. Each step is a bounded sample: HOST_SAMPLE of the 32 sequences,
+    rotating so that consecutive steps cover all of them; a sequence's host cost
+    does not depend on which others share its step, so tokens/s is the rate of
+    the whole step."""
     if rank != 0:
         return None
-    import oracle
-    from a11spec import workloads as W
-    st = W.make_c5(seed=5, batch=B_PER_GPU, ctx=CTX, device="cpu")
-    hs = host_state(st)
-    threads = os.cpu_count() or 1
+    W = workloads_module()
+    threads = len(os.sched_getaffinity(0))
     torch.set_num_threads(threads)
-    ref_built = oracle.ref() is not None
-    for i in range(args.warmup):
-        cpu_path_one_sequence(hs, i % B_PER_GPU, ref_built)
+    st = host_state(W.make_c5(seed=5, batch=B_PER_GPU, ctx=CTX, device="cpu", spare_pages=SPARE_PAGES))
+    path = HostStep(st)
+
+    def seqs(k):
+        return [(k * HOST_SAMPLE + i) % B_PER_GPU for i in range(HOST_SAMPLE)]
+
+    for k in range(args.warmup):
+        path.step(seqs(k))
     t0 = time.perf_counter()
     emitted = 0
-    for i in range(args.steps):
-        emitted += cpu_path_one_sequence(hs, i % B_PER_GPU, ref_built)
+    for k in range(args.steps):
+        emitted += path.step(seqs(args.warmup + k))
     dt = time.perf_counter() - t0
     v = emitted / dt
     return {"metric": METRIC, "value": v, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "impl": "reference",
-            "data": "synthetic (seeded)",
-            "config": {"workload": "C5 end-to-end, one sequence per step (bounded sample)",
-                       "ctx": CTX, "max_nodes": MAX_NODES, "vocab": VOCAB},
-            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads,
-                             "kind": "reference" if ref_built else "port",
-                             "sample": "one sequence of the 32-sequence per-GPU workload per step"},
+            "data": "synthetic (seeded; no dataset exists for this path)",
+            "config": workload_config(world),
+            "cpu_baseline": {"value": v, "unit": UNIT, "cores": threads, "kind": path.kind,
+                             "sample": f"each step {HOST_SAMPLE} of the {B_PER_GPU} sequences of the per-GPU "
+                                       f"step, rotating over all of them; trigram expansion (oracle), attention, "
+                                       f"LM head and sampler in torch fp32, acceptance by the "
+                                       f"{'reference verifier' if path.kind == 'reference' else 'oracle'}"},
             "e2e": {"value": v, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -465,6 +742,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true")
     args = ap.parse_args()
     # The JSON line is the only thing on stdout: file descriptor 1 points at
     # stderr for the run (libraries such as NCCL print banners there) and the

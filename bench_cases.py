@@ -1,10 +1,10 @@
 """Seeded single-kernel cases for timing and profiling.
 
-    python a11-llm-optimizer_b200/a11spec/cases.py attention --batch 16 --ctx 4096 --iters 2
-    python a11-llm-optimizer_b200/a11spec/cases.py accept --mode onehot --batch 32 --iters 2
-    python a11-llm-optimizer_b200/a11spec/cases.py compact --batch 32 --ctx 4096 --iters 2
-    python a11-llm-optimizer_b200/a11spec/cases.py ngram --batch 32 --iters 2
-    python a11-llm-optimizer_b200/a11spec/cases.py pages --batch 32 --ctx 32768 --iters 20
+    python bench_cases.py attention --batch 16 --ctx 4096 --iters 2
+    python bench_cases.py accept --mode onehot --batch 32 --iters 2
+    python bench_cases.py compact --batch 32 --ctx 4096 --iters 2
+    python bench_cases.py ngram --batch 32 --iters 2
+    python bench_cases.py pages --batch 32 --ctx 32768 --iters 20
 
 Each case builds its inputs on cuda:0 (seeded), runs the kernel `--warmup`
 times, then `--iters` times between CUDA events, and prints one JSON line
@@ -19,8 +19,7 @@ import json
 import os
 import sys
 
-if __package__ in (None, ""):
-    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+sys.path.insert(0, os.path.join(os.path.dirname(os.path.abspath(__file__)), "a11-llm-optimizer_b200"))
 
 import numpy as np
 import torch

@@ -164,13 +164,16 @@ int a11s_verify_chain(const float *draft_probs, const float *target_probs, const
  * synchronisation. The scratch is one file-scope device array of
  * A11S_ACCEPT_STATIC_SCRATCH_BYTES (4 MiB) that every GPU loading the library
  * holds until the process exits; calls whose a11s_accept_workspace_bytes()
- * exceeds it return A11S_ENOSPACE. The first call on a device looks up that
- * array's device address (cudaGetSymbolAddress); make that first call before
- * any stream capture. All calls share the array: calls that overlap on the GPU
- * (other streams, other host threads) race and must be serialised by the
- * caller. Arguments and results are those of a11s_accept; `status` (nullable,
- * device int32[2]) receives the device status word and its detail. Allocates
- * nothing (no cudaMalloc, cudaFree or allocating library routine). */
+ * exceeds it return A11S_ENOSPACE, with the largest batch that fits in the
+ * message. Every call looks up the array's device address in the context
+ * current at the call (cudaGetSymbolAddress); the first lookup on a device may
+ * load the library's device code, so make the first call before any stream
+ * capture. All calls share the array: calls that overlap on the GPU (other
+ * streams, other host threads) race and must be serialised by the caller.
+ * Arguments and results are those of a11s_accept; `status` (nullable, device
+ * int32[2]) receives the device status word and its detail, stream-ordered
+ * after the kernel ({0, 0} for an empty batch). Allocates nothing (no
+ * cudaMalloc, cudaFree or allocating library routine). */
 #define A11S_ACCEPT_STATIC_SCRATCH_BYTES (4u << 20)
 int a11s_accept_static(int32_t mode, int32_t dtype,
                        const void *target_logits, const void *draft_logits, int64_t row_stride,

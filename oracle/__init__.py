@@ -45,11 +45,19 @@ def build(force: bool = False) -> str:
     return LIB_PATH
 
 
-def build_ref(ref_root: str = "/root/reference") -> bool:
-    """Compile the reference verifier into _ref/ if its sources are present."""
-    if not os.path.isdir(os.path.join(ref_root, "src", "engine")):
+def build_ref(ref_root: str | None = None) -> bool:
+    """Compile the reference verifier into _ref/ from the reference tree at
+    `ref_root` (default: the A11_REFERENCE_ROOT environment variable). Returns
+    False, building nothing, when no tree is given or its sources are absent."""
+    ref_root = ref_root or os.environ.get("A11_REFERENCE_ROOT")
+    if not ref_root or not os.path.isdir(os.path.join(ref_root, "src", "engine")):
         return False
     subprocess.run(["make", "-s", "-C", HERE, "ref", f"REF={ref_root}"], check=True)
+    # The reference's binding tests, compiled unchanged to bytecode, so a GPU
+    # machine without the reference tree can run them against a11_optimizer.
+    import py_compile
+    py_compile.compile(os.path.join(ref_root, "tests", "test_python_bindings.py"),
+                       cfile=os.path.join(HERE, "_ref", "test_python_bindings.pyc"), doraise=True)
     return True
 
 

@@ -13,7 +13,7 @@ are read from that file at generation time and executed on the tensors. A
 chain-shaped draft tree is exactly the reference's token-by-token decode: node
 i attends to the context and nodes 0..i.
 
-    python tests/golden/make_golden.py
+    A11_REFERENCE_ROOT=<reference tree> python tests/golden/make_golden.py
 """
 import json
 import os
@@ -74,7 +74,8 @@ def ref_chains():
                      "thread_local mt19937(42) stream (u)")
 
 
-REF = os.environ.get("A11_REFERENCE", "/root/reference")
+# The reference tree's location; no default. Only the generation below reads it.
+REF = os.environ.get("A11_REFERENCE_ROOT", "")
 
 
 def _reference_attention_statements():
@@ -160,8 +161,10 @@ def sampler_logits(seed, vocab):
 
 
 if __name__ == "__main__":
+    if not REF or not os.path.isdir(os.path.join(REF, "engine")):
+        sys.exit("make_golden.py: set A11_REFERENCE_ROOT to the reference tree (its engine/ and src/ are read)")
     oracle.build()
-    if not oracle.build_ref():
+    if not oracle.build_ref(REF):
         sys.exit("reference tree not found: golden fixtures need the reference verifier")
     with open(os.path.join(HERE, "c1_greedy_chain.json"), "w") as f:
         json.dump(c1(), f, indent=1)

@@ -154,6 +154,32 @@ def test_reference_catch2_suite_against_cpp_adapter(dev):
     assert "All tests passed" in r.stdout
 
 
+def test_reference_python_binding_tests_against_a11_optimizer(dev):
+    """The reference's tests/test_python_bindings.py, unchanged (compiled to
+    bytecode from the reference tree at build time), against the module
+    a11_optimizer of this repository: its module constants, PagedKVCacheManager,
+    SpeculativeTreeVerifier (:166-275) and cross-class cases. The NvmeAsyncLoader
+    cases belong to weight streaming, which this library does not provide."""
+    import importlib.machinery
+    import importlib.util
+
+    import a11_optimizer
+    pyc = os.path.join(ROOT, "oracle", "_ref", "test_python_bindings.pyc")
+    if not os.path.exists(pyc):
+        pytest.skip("reference binding tests not compiled (needs the reference tree at build time)")
+    loader = importlib.machinery.SourcelessFileLoader("ref_test_python_bindings", pyc)
+    mod = importlib.util.module_from_spec(importlib.util.spec_from_loader(loader.name, loader))
+    loader.exec_module(mod)
+    ran = []
+    for cls_name in ("TestModuleConstants", "TestPagedKVCacheManager", "TestSpeculativeTreeVerifier",
+                     "TestCrossClassIntegration"):
+        cls = getattr(mod, cls_name)
+        for name in sorted(n for n in dir(cls) if n.startswith("test_")):
+            getattr(cls(), name)(a11_optimizer)
+            ran.append(f"{cls_name}.{name}")
+    assert len(ran) == 3 + 7 + 9 + 1, ran
+
+
 # ----------------------------------------------------------------------------- SpeculativeDecoder
 def test_decoder_list_api_and_step(dev):
     V = 4096
