@@ -134,7 +134,7 @@ def test_static_scratch_full_array_and_one_more(dev, mode):
     f = _bind()
     N, V = 64, 151936
     B = _largest_batch(mode, N, V)
-    assert a11spec.ops.accept_workspace_bytes(mode, B, N, V) > (4 << 20) - 4096  # near the top
+    assert a11spec.ops.accept_workspace_bytes(mode, B, N, V) > 0.95 * (4 << 20)  # the top end of the array
     _compare_at(f, mode, B, N, V, seed=31 + mode)
     z = torch.zeros(1, dtype=torch.int32, device="cuda")
     logits = torch.zeros(8, dtype=torch.bfloat16, device="cuda")  # never read
