@@ -20,8 +20,9 @@ target forward.
 
 The target model is any object with:
 
-* ``vocab`` (int), ``k_pool`` / ``v_pool`` (bf16 [pages, 16, Hkv, D], the
-  paged KV cache the model's attention reads);
+* ``vocab`` (int), ``k_pool`` / ``v_pool`` (bf16 [pages, 16, Hkv, D], or
+  [num_layers, pages, 16, Hkv, D] with a ``num_layers`` attribute: the paged KV
+  cache the model's attention reads, one slab per layer);
 * ``prefill(tokens, page_table, ctx_lens)``: write the K/V of tokens
   [B, T] at positions 0 .. T-1 (ctx_lens is 0 on entry; the caller sets it);
 * ``forward_tree(tokens, parents, n_nodes, page_table, ctx_lens)`` ->
@@ -70,7 +71,8 @@ def speculative_stream(model, prompts: torch.Tensor, max_new_tokens: int, decode
         uni = uniforms_fn(B, N) if (uniforms_fn is not None and decoder.temperature is not None) else None
         res = decoder.verify(tree, logits, uniforms=uni)  # draws its own uniforms when sampling without them
         freed, n_freed = ops.kv_compact(model.k_pool, model.v_pool, page_table, ctx_lens, res.accept_len,
-                                        res.accepted_nodes, tree.n_nodes)
+                                        res.accepted_nodes, tree.n_nodes,
+                                        num_layers=getattr(model, "num_layers", 1))
         pages.release(freed, n_freed)
         # next root pair (last accepted token, or the old root; bonus) and, when
         # learning, the committed-token rows built from the old pair: one launch

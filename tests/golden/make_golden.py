@@ -123,6 +123,64 @@ def attn_chains():
     return out
 
 
+TREE_DECODER = dict(n_layers=2, n_embd=256, n_head=8, n_head_kv=1, head_dim=128, n_ff=512, vocab=512)
+TREE_DECODER_SEED = 7
+TREE_DECODER_STEPS = 40
+
+
+def tree_decoder_decode():
+    """Greedy decode of a small synthetic decoder by the reference's own
+    A11Pipeline.forward_token / forward_layer (engine/pipeline.py:350-473, its
+    dense SwiGLU branch, bf16 compute, its KVCacheManager holding the keys and
+    values), on the seeded weights of a11spec.tree_model.synthetic_tensors.
+    The prompt is the first of a seeded series whose first 20 greedy steps all
+    have a top-2 logit gap of at least 0.1 (bf16 logits tie often; a gap that
+    wide cannot be closed by rounding differences between machines), and 40
+    steps are recorded with their logits and gaps."""
+    import types
+    import torch
+    sys.path.insert(0, REF)
+    from engine.kv_cache import KVCacheManager  # the reference's KV cache
+    from engine.pipeline import A11Pipeline  # the reference's decoder (its methods run unchanged)
+    from a11spec.tree_model import DecoderConfig, synthetic_tensors
+    cfg = DecoderConfig(**TREE_DECODER)
+    tensors = synthetic_tensors(cfg, TREE_DECODER_SEED)
+
+    def reference_pipeline():
+        pipe = A11Pipeline.__new__(A11Pipeline)  # no model files: the decoder state only
+        pipe.config = types.SimpleNamespace(n_head=cfg.n_head, n_head_kv=cfg.n_head_kv, head_dim=cfg.head_dim,
+                                            rms_eps=cfg.rms_eps, rope_base=cfg.rope_base)
+        pipe.weights = types.SimpleNamespace(get_torch=lambda name: tensors[name])
+        pipe.loader = types.SimpleNamespace(tensors=dict.fromkeys(tensors))
+        pipe.kv_cache_manager = KVCacheManager(n_layers=cfg.n_layers, n_head_kv=cfg.n_head_kv,
+                                               head_dim=cfg.head_dim, page_size=16)
+        pipe.device = torch.device("cpu")
+        pipe.compute_dtype = torch.bfloat16
+        pipe.num_layers = cfg.n_layers
+        return pipe
+
+    for prompt_seed in range(100):
+        prompt = np.random.default_rng(prompt_seed).integers(0, cfg.vocab, 6).astype(np.int32)
+        pipe = reference_pipeline()
+        for pos, tok in enumerate(prompt[:-1]):
+            pipe.forward_token(int(tok), pos)
+        tok, pos = int(prompt[-1]), len(prompt) - 1
+        out, rows, gaps = [], [], []
+        for _ in range(TREE_DECODER_STEPS):
+            logits = pipe.forward_token(tok, pos).float()
+            top = torch.topk(logits, 2).values
+            gaps.append(float(top[0] - top[1]))
+            rows.append(logits.numpy())
+            tok = int(torch.argmax(logits))
+            out.append(tok)
+            pos += 1
+        if min(gaps[:20]) >= 0.1:
+            return dict(prompt=prompt, tokens=np.array(out, np.int32), logits=np.stack(rows).astype(np.float32),
+                        gaps=np.array(gaps, np.float32), prompt_seed=np.int32(prompt_seed),
+                        weight_seed=np.int32(TREE_DECODER_SEED))
+    raise RuntimeError("no prompt with 20 well-separated greedy steps")
+
+
 def sampler_probs():
     """Probabilities of the reference's TokenSampler (engine/sampler.py) with
     top-k and top-p off, i.e. softmax(logits / max(T, 1e-5)): the sampler
@@ -173,4 +231,5 @@ if __name__ == "__main__":
     np.savez_compressed(os.path.join(HERE, "attn_chains.npz"), **attn_chains())
     with open(os.path.join(HERE, "sampler_probs.json"), "w") as f:
         json.dump(sampler_probs(), f, indent=1)
+    np.savez_compressed(os.path.join(HERE, "tree_decoder_decode.npz"), **tree_decoder_decode())
     print("golden fixtures written")
