@@ -64,65 +64,128 @@ struct Vec {
     }
 };
 
-// Chunk max of one row chunk, lane layout: vector i of lane = logits
-// [(i*32 + lane) * EPV, +EPV). Positions past the row are -inf.
-template <bool BF16>
-__device__ __forceinline__ float chunk_max(const char *row, int c0, int clen, int lane) {
-    using VT = Vec<BF16>;
-    constexpr int G = 8;  // vectors in flight per lane
-    float m = -INFINITY;
+// bf16 rows: the whole chunk sits in a lane's registers, 8 vectors of 8
+// logits (vector g of lane = logits [(g*32 + lane) * 8, +8)); positions past
+// the row read as -inf. The vocab is a multiple of 8, so a vector is either
+// wholly inside the row or wholly past it.
+__device__ __forceinline__ void load_chunk_bf16(const char *row, int c0, int clen, int lane, uint4 (&d)[8]) {
 #pragma unroll
-    for (int i0 = 0; i0 < VT::NV; i0 += G) {
-        uint4 d[G];
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
-            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
-            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
-        }
-#pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int e = 0; e < VT::EPV; ++e) m = max_nan(m, VT::at(d[g], e));
+    for (int g = 0; g < 8; ++g) {
+        const int e0 = (g * 32 + lane) * 8;
+        d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * 2) : make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
     }
-    return warp_max_nan(m);
 }
 
-// Chunk max (as chunk_max) and the first position in the chunk holding it:
-// each lane keeps its running maximum with the first position reaching it
-// (its positions increase along its reads; a NaN never replaces the first
-// value, and a chunk holding a NaN has a NaN maximum whose position is never
-// asked for), then the warp takes the smallest position among the lanes
-// whose maximum equals the chunk's.
+// NaN-propagating maximum of two packed bf16 pairs. The maximum of bf16
+// values is one of them, so taking it on the packed halves and widening once
+// gives exactly the maximum of the widened values (a NaN stays a NaN).
+__device__ __forceinline__ uint32_t max_nan_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+__device__ __forceinline__ uint32_t vec_max_bf16x2(const uint4 &d) {
+    return max_nan_bf16x2(max_nan_bf16x2(d.x, d.y), max_nan_bf16x2(d.z, d.w));
+}
+
+// Chunk max of one row chunk, lane layout: vector i of lane = logits
+// [(i*32 + lane) * EPV, +EPV). Positions past the row are -inf. bf16 rows take
+// the maximum on packed pairs (four instructions per 16-byte vector).
+template <bool BF16>
+__device__ __forceinline__ float chunk_max(const char *row, int c0, int clen, int lane) {
+    if constexpr (BF16) {
+        uint4 d[8];
+        load_chunk_bf16(row, c0, clen, lane, d);
+        uint32_t m2 = vec_max_bf16x2(d[0]);
+#pragma unroll
+        for (int g = 1; g < 8; ++g) m2 = max_nan_bf16x2(m2, vec_max_bf16x2(d[g]));
+        return warp_max_nan(max_nan(bf16lo(m2), bf16hi(m2)));
+    } else {
+        using VT = Vec<BF16>;
+        constexpr int G = 8;  // vectors in flight per lane
+        float m = -INFINITY;
+#pragma unroll
+        for (int i0 = 0; i0 < VT::NV; i0 += G) {
+            uint4 d[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+                d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ)
+                                 : make_uint4(0xFF800000u, 0xFF800000u, 0xFF800000u, 0xFF800000u);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int e = 0; e < VT::EPV; ++e) m = max_nan(m, VT::at(d[g], e));
+        }
+        return warp_max_nan(m);
+    }
+}
+
+// Chunk max (as chunk_max) and the first position in the chunk holding it
+// (float equality, so -0 and +0 are the same value, as argmax sees them; a
+// chunk holding a NaN has a NaN maximum whose position is never asked for).
+// bf16: every lane takes its packed maximum; only the lanes whose maximum is
+// the chunk's search their registers, vector by vector, for its first
+// position, and the warp takes the smallest. fp32: each lane keeps its first
+// strictly greater value along its reads, then the warp takes the smallest
+// position among the lanes whose maximum equals the chunk's.
 template <bool BF16>
 __device__ __forceinline__ float chunk_max_first(const char *row, int c0, int clen, int lane, int &first) {
-    using VT = Vec<BF16>;
-    constexpr int G = 8;
-    float m = -INFINITY, bv = -INFINITY;
-    int bi = INT_MAX;
+    if constexpr (BF16) {
+        uint4 d[8];
+        load_chunk_bf16(row, c0, clen, lane, d);
+        uint32_t vm[8];
 #pragma unroll
-    for (int i0 = 0; i0 < VT::NV; i0 += G) {
-        uint4 d[G];
+        for (int g = 0; g < 8; ++g) vm[g] = vec_max_bf16x2(d[g]);
+        const uint32_t m2 = max_nan_bf16x2(max_nan_bf16x2(max_nan_bf16x2(vm[0], vm[1]), max_nan_bf16x2(vm[2], vm[3])),
+                                           max_nan_bf16x2(max_nan_bf16x2(vm[4], vm[5]), max_nan_bf16x2(vm[6], vm[7])));
+        const float ml = max_nan(bf16lo(m2), bf16hi(m2));
+        const float M = warp_max_nan(ml);
+        int f = INT_MAX;
+        if (ml == M) {  // this lane holds the chunk maximum (never when it is NaN)
 #pragma unroll
-        for (int g = 0; g < G; ++g) {
-            const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
-            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
-            d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ) : make_uint4(ninf, ninf, ninf, ninf);
-        }
+            for (int g = 0; g < 8; ++g) {
+                if (f == INT_MAX && max_nan(bf16lo(vm[g]), bf16hi(vm[g])) == M) {
 #pragma unroll
-        for (int g = 0; g < G; ++g)
-#pragma unroll
-            for (int e = 0; e < VT::EPV; ++e) {
-                const float v = VT::at(d[g], e);
-                const int pos = ((i0 + g) * 32 + lane) * VT::EPV + e;
-                m = max_nan(m, v);
-                if (pos < clen && (bi == INT_MAX || v > bv)) { bv = v; bi = pos; }
+                    for (int e = 0; e < 8; ++e) {
+                        const int pos = (g * 32 + lane) * 8 + e;
+                        if (f == INT_MAX && pos < clen && Vec<true>::at(d[g], e) == M) f = pos;
+                    }
+                }
             }
+        }
+        first = -warp_max(-f);  // warp min
+        return M;
+    } else {
+        using VT = Vec<BF16>;
+        constexpr int G = 8;
+        float m = -INFINITY, bv = -INFINITY;
+        int bi = INT_MAX;
+#pragma unroll
+        for (int i0 = 0; i0 < VT::NV; i0 += G) {
+            uint4 d[G];
+#pragma unroll
+            for (int g = 0; g < G; ++g) {
+                const int e0 = ((i0 + g) * 32 + lane) * VT::EPV;
+                d[g] = e0 < clen ? ldg_stream(row + (size_t)(c0 + e0) * VT::ESZ)
+                                 : make_uint4(0xFF800000u, 0xFF800000u, 0xFF800000u, 0xFF800000u);
+            }
+#pragma unroll
+            for (int g = 0; g < G; ++g)
+#pragma unroll
+                for (int e = 0; e < VT::EPV; ++e) {
+                    const float v = VT::at(d[g], e);
+                    const int pos = ((i0 + g) * 32 + lane) * VT::EPV + e;
+                    m = max_nan(m, v);
+                    if (pos < clen && (bi == INT_MAX || v > bv)) { bv = v; bi = pos; }
+                }
+        }
+        m = warp_max_nan(m);
+        int f = (bi != INT_MAX && bv == m) ? bi : INT_MAX;
+        first = -warp_max(-f);  // warp min
+        return m;
     }
-    m = warp_max_nan(m);
-    int f = (bi != INT_MAX && bv == m) ? bi : INT_MAX;
-    first = -warp_max(-f);  // warp min
-    return m;
 }
 
 // Sum of fixed-point weights of one chunk in frame cf (no max needed: the
@@ -194,6 +257,8 @@ struct WalkSmem {
     RowStat ps, qs;
     uint64_t S_eff, bt2;
     int32_t nexcl, L, node, alen, ck, nk, action, child, ok, bj, res[2];
+    uint32_t gen;         // generation of this walk's latest residual pass (DRAFT)
+    int32_t no_helpers;   // set when a pass's wait ran out: later passes stay in this block
 };
 
 // Inverse CDF inside one chunk, every thread of the block: thread t owns the
@@ -406,6 +471,197 @@ __device__ __forceinline__ uint64_t level_weight(float p_prev, float q) {
     return __float2ull_rz(__fmul_rn(r, 0x1p40f));
 }
 
+// One chunk of a residual pass (STOCH_DRAFT), one warp: the sum over the chunk
+// of level_weight(p_L(v), q(v)), where p_L is p after the L residual levels
+// of invT (p and q in their row frames: fp/fq, scales scp/scq). Four vectors of
+// p and q in flight per lane. Every lane returns the warp's sum.
+template <bool BF16>
+__device__ uint64_t resid_chunk_sum(const char *prow, const char *qrow, int c0, int clen, float k, int32_t fp,
+                                    int32_t fq, double scp, double scq, int L, const double *invT, int lane) {
+    constexpr int EPV = Vec<BF16>::EPV, NV = Vec<BF16>::NV, G = 4;
+    uint64_t s = 0;
+    for (int i0 = 0; i0 < NV; i0 += G) {
+        uint4 vp[G], vq[G];
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+            const int e0 = ((i0 + g) * 32 + lane) * EPV;
+            const size_t off = (size_t)(c0 + e0) * (BF16 ? 2 : 4);
+            const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
+            vp[g] = e0 < clen ? ldg_stream(prow + off) : make_uint4(ninf, ninf, ninf, ninf);
+            vq[g] = e0 < clen ? ldg_stream(qrow + off) : make_uint4(ninf, ninf, ninf, ninf);
+        }
+#pragma unroll
+        for (int g = 0; g < G; ++g)
+#pragma unroll
+            for (int e = 0; e < EPV; ++e) {
+                const float pv = prob_of(Vec<BF16>::at(vp[g], e), k, fp, scp);
+                const float qv = prob_of(Vec<BF16>::at(vq[g], e), k, fq, scq);
+                s += level_weight(level_prob(pv, qv, L, invT), qv);
+            }
+    }
+    return warp_sum_u64(s);
+}
+
+// A pass over one visited row of a walk, shared with helper blocks (sampling
+// modes), one at a time per sequence:
+//   kind 0 (STOCH_DRAFT): the chunk totals of the next residual level,
+//          sum over the chunk of level_weight(p_L(v), q(v)), into sums[j];
+//   kind 1: the row statistics of a recorded row: each chunk's frame (from
+//          its bulk-pass maximum) and weight sum, for the p row (fr, sums) and
+//          in STOCH_DRAFT the q row (qfr, qsums).
+// The walking block publishes the pass (kind, visited node, level L, row
+// statistics, frames, invT) and opens it by writing `word` = (generation << 32)
+// | 0. A block (the walker or a helper) takes chunks for its warps by adding
+// their number to `word` (one atomic per claim); the value the add returns
+// names the pass and the first chunk taken, so a claim never takes a chunk of
+// another pass. Each warp computes its chunk, stores the results and counts
+// the chunk in `done`. The walker publishes the next pass only after `done`
+// reached the chunk count of the last, so no late write lands in a newer pass.
+// The walker claims chunks too, so a pass finishes even when no helper runs.
+struct SharedPass {
+    unsigned long long word;  // generation << 32 | chunks claimed (0: no pass yet)
+    int32_t done;             // chunks whose results are stored, this generation
+    int32_t node, L, kind;
+    RowStat ps, qs;
+    double invT[A11S_MAX_WALK_LEVELS + 1];
+};
+constexpr size_t kJobHead = (sizeof(SharedPass) + 255) & ~size_t(255);
+size_t accept_job_bytes(int nch) { return kJobHead + (size_t)nch * 2 * (sizeof(int32_t) + sizeof(uint64_t)); }
+__device__ __forceinline__ SharedPass *job_of(const AcceptArgs &a, int b) {
+    return reinterpret_cast<SharedPass *>(a.jobs + (size_t)b * a.job_stride);
+}
+__device__ __forceinline__ int32_t *job_fr(const AcceptArgs &a, int b) {
+    return reinterpret_cast<int32_t *>(a.jobs + (size_t)b * a.job_stride + kJobHead);
+}
+__device__ __forceinline__ int32_t *job_qfr(const AcceptArgs &a, int b) { return job_fr(a, b) + a.nch; }
+__device__ __forceinline__ unsigned long long *job_sums(const AcceptArgs &a, int b) {
+    return reinterpret_cast<unsigned long long *>(job_fr(a, b) + 2 * a.nch);
+}
+__device__ __forceinline__ unsigned long long *job_qsums(const AcceptArgs &a, int b) { return job_sums(a, b) + a.nch; }
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const void *p) {
+    unsigned long long v;
+    asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+// Claim up to `want` chunks of pass `gen` (one thread): returns the first
+// chunk and sets *count (0 when every chunk is taken or the pass is no longer
+// the open one). An add that finds the pass exhausted only raises its claimed
+// count past the chunk count, which changes nothing.
+__device__ int claim_chunks(unsigned long long *word, uint32_t gen, int nch, int want, int *count) {
+    *count = 0;
+    const unsigned long long w = ld_relaxed_u64(word);
+    if ((uint32_t)(w >> 32) != gen || (uint32_t)w >= (uint32_t)nch) return -1;
+    const unsigned long long old = atomicAdd(word, (unsigned long long)want);
+    if ((uint32_t)(old >> 32) != gen || (uint32_t)old >= (uint32_t)nch) return -1;
+    const int j0 = (int)(uint32_t)old;
+    *count = min(want, nch - j0);
+    return j0;
+}
+constexpr long long kHelperBudget = 20000000ll;   // ~10 ms of SM clock: helpers leave after it whatever happens
+constexpr long long kPassWaitBudget = 4000000ll;  // ~2 ms: a walker's wait for its helpers' last chunks
+
+// One chunk j of sequence b's open pass (one warp); stores the results and
+// counts the chunk done. invT: the pass's residual levels (kind 0).
+template <int MODE, bool BF16>
+__device__ void pass_chunk(const AcceptArgs &a, int b, int kind, int node, int L, const RowStat &ps,
+                           const RowStat &qs, const double *invT, int j, int lane) {
+    const size_t row_bytes = (size_t)a.stride * (BF16 ? 2 : 4);
+    const char *prow = reinterpret_cast<const char *>(a.target) + ((size_t)b * a.N + node) * row_bytes;
+    const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT
+                           ? reinterpret_cast<const char *>(a.draft) + ((size_t)b * a.N + node) * row_bytes
+                           : nullptr;
+    const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, a.V - c0);
+    SharedPass *job = job_of(a, b);
+    if (kind == 0) {
+        if constexpr (MODE == A11S_ACCEPT_STOCH_DRAFT) {
+            const int32_t fp = __ldcg(job_fr(a, b) + j), fq = __ldcg(job_qfr(a, b) + j);
+            const uint64_t sum = resid_chunk_sum<BF16>(prow, qrow, c0, clen, a.k, fp, fq, chunk_scale(ps, fp),
+                                                       chunk_scale(qs, fq), L, invT, lane);
+            if (lane == 0) __stcg(job_sums(a, b) + j, (unsigned long long)sum);
+        }
+    } else {
+        // the row's frames from its bulk-pass maxima, then its weights
+        const int nrows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
+        int bad = 0;
+        for (int q = 0; q < nrows; ++q) {
+            const int r = q ? a.N + node : node;
+            const float cm = __ldcg(a.recs + ((size_t)b * a.rows_per_seq + r) * a.nch + j);
+            bad |= !(cm < INFINITY) || (cm > -INFINITY && !(fabsf(__fmul_rn(cm, a.k)) < 16777216.0f));
+            const int32_t f = cm < INFINITY ? frame_of(cm, a.k) : A11S_FRAME_NONE;
+            const uint64_t s = f == A11S_FRAME_NONE ? 0ull : chunk_wsum<BF16>(q ? qrow : prow, c0, clen, a.k, (float)f, lane);
+            if (lane == 0) {
+                __stcg(reinterpret_cast<int *>((q ? job_qfr(a, b) : job_fr(a, b)) + j), (int)f);
+                __stcg((q ? job_qsums(a, b) : job_sums(a, b)) + j, (unsigned long long)s);
+            }
+        }
+        if (bad && lane == 0) report(a.status, A11S_ENONFINITE, b);
+    }
+    if (lane == 0) {
+        __threadfence();
+        atomicAdd(&job->done, 1);
+    }
+}
+
+// Helper blocks (grid rows >= bulk_rows, sampling modes): thread 0 looks for
+// an open pass with unclaimed chunks, starting at a sequence of its own, and
+// claims one chunk per warp; each warp computes its chunk. The block leaves
+// once every walk has finished (or its budget ran out). A pass's parameters
+// were written before it was opened; they are read from L2 after the claim.
+template <int MODE, bool BF16>
+__device__ void pass_helper(const AcceptArgs &a, int warp, int lane) {
+    __shared__ double s_invT[A11S_MAX_WALK_LEVELS + 1];
+    __shared__ int s_b, s_j0, s_n;
+    const long long t0 = clock64();
+    int start = (int)(blockIdx.x + (blockIdx.y - a.bulk_rows) * gridDim.x) % a.B;
+    for (;;) {
+        if (threadIdx.x == 0) {
+            int b = -1, j0 = -1, n = 0;
+            if (ld_relaxed(a.walkers_done) >= (uint32_t)a.B || clock64() - t0 > kHelperBudget) {
+                b = -2;
+            } else {
+                for (int t = 0; t < a.B && n == 0; ++t) {
+                    const int bb = (start + t) % a.B;
+                    SharedPass *job = job_of(a, bb);
+                    const unsigned long long w = ld_relaxed_u64(&job->word);
+                    const uint32_t g = (uint32_t)(w >> 32);
+                    if (g == 0) continue;
+                    j0 = claim_chunks(&job->word, g, a.nch, kWarps, &n);
+                    if (n) b = bb;
+                }
+            }
+            s_b = b;
+            s_j0 = j0;
+            s_n = n;
+            if (b >= 0) start = b;  // stay with this pass while it has chunks
+        }
+        __syncthreads();
+        const int b = s_b, j0 = s_j0, n = s_n;
+        if (b == -2) return;
+        if (n == 0) {
+            __syncthreads();
+            if (threadIdx.x == 0) __nanosleep(512);
+            continue;
+        }
+        __threadfence();
+        SharedPass *job = job_of(a, b);
+        const int kind = __ldcg(&job->kind), node = __ldcg(&job->node), L = __ldcg(&job->L);
+        if (kind == 0)
+            for (int l = threadIdx.x; l <= L; l += blockDim.x) s_invT[l] = __ldcg(&job->invT[l]);
+        __syncthreads();
+        if (warp < n) {
+            RowStat ps, qs;
+            ps.C = __ldcg(&job->ps.C);
+            ps.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->ps.S));
+            ps.invS = __ldcg(&job->ps.invS);
+            qs.C = __ldcg(&job->qs.C);
+            qs.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->qs.S));
+            qs.invS = __ldcg(&job->qs.invS);
+            pass_chunk<MODE, BF16>(a, b, kind, node, L, ps, qs, s_invT, j0 + warp, lane);
+        }
+        __syncthreads();  // s_invT and the claim are reused
+    }
+}
+
 // Warp 0 copies one chunk of a row into shared memory as fp32 (coalesced
 // 16-byte loads, all in flight together); positions past the row get -inf.
 template <bool BF16>
@@ -541,6 +797,10 @@ __device__ int row_argmax_rec(const float *cmax, const int32_t *arg, int nch, in
 template <int MODE, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if ((int)blockIdx.y >= a.bulk_rows) {  // helper block (sampling modes only)
+        if constexpr (MODE != A11S_ACCEPT_GREEDY) pass_helper<MODE, BF16>(a, warp, lane);
+        return;
+    }
     int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
     const bool seq_ok = n_live >= 1 && n_live <= a.N;
     if (!seq_ok) n_live = 0;
@@ -631,7 +891,88 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         sm.par[i] = a.parents[(size_t)b * N + i];
         if (MODE != A11S_ACCEPT_GREEDY) sm.uni[i] = a.uniforms[(size_t)b * N + i];
     }
+    if (threadIdx.x == 0) {
+        sm.gen = 0;
+        sm.no_helpers = a.jobs ? 0 : 1;
+    }
     __syncthreads();
+    // A pass over visited node nd's rows shared with the helper blocks (see
+    // SharedPass), every thread: publish, take chunks alongside the helpers,
+    // wait (bounded) for the helpers' last chunks. False when this walk no
+    // longer shares its passes (a wait ran out once): the caller computes the
+    // pass in this block. Kind 0 reads sm.fr / sm.qfr / sm.invT / sm.L and the
+    // row statistics sm.ps / sm.qs.
+    auto run_pass = [&](int kind, int nd) -> bool {
+        if (sm.no_helpers) return false;
+        SharedPass *job = job_of(a, b);
+        if (kind == 0) {
+            int32_t *jfr = job_fr(a, b), *jqfr = job_qfr(a, b);
+            for (int j = threadIdx.x; j < nch; j += blockDim.x) { jfr[j] = sm.fr[j]; jqfr[j] = sm.qfr[j]; }
+            for (int l = threadIdx.x; l <= sm.L; l += blockDim.x) job->invT[l] = sm.invT[l];
+        }
+        if (threadIdx.x == 0) {
+            job->done = 0;
+            job->node = nd;
+            job->L = sm.L;
+            job->kind = kind;
+            job->ps = sm.ps;
+            job->qs = sm.qs;
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            sm.gen += 1;
+            atomicExch(&job->word, (unsigned long long)sm.gen << 32);  // open the pass
+        }
+        __syncthreads();
+        const uint32_t gen = sm.gen;
+        const int L = sm.L;
+        const RowStat ps = sm.ps, qs = sm.qs;
+        for (;;) {  // this block takes chunks too, one per warp
+            if (threadIdx.x == 0) {
+                int n = 0;
+                const int j0 = claim_chunks(&job->word, gen, nch, kWarps, &n);
+                sm.res[0] = j0;
+                sm.res[1] = n;
+            }
+            __syncthreads();
+            const int j0 = sm.res[0], n = sm.res[1];
+            __syncthreads();  // sm.res is read by every thread before it changes
+            if (n == 0) break;
+            if (warp < n) pass_chunk<MODE, BF16>(a, b, kind, nd, L, ps, qs, sm.invT, j0 + warp, lane);
+        }
+        if (threadIdx.x == 0) {  // the helpers' last chunks (bounded wait)
+            const long long t0 = clock64();
+            bool all = false;
+            while (!(all = ld_relaxed(&job->done) >= (uint32_t)nch)) {
+                if (clock64() - t0 > kPassWaitBudget) break;
+                __nanosleep(128);
+            }
+            if (!all) {
+                // never reuse this pass slot (a late chunk could land in a newer
+                // pass): close it and compute the rest of the walk in this block
+                atomicExch(&job->word, ((unsigned long long)gen << 32) | 0xFFFFFFFFull);
+                sm.no_helpers = 1;
+            }
+            __threadfence();
+        }
+        __syncthreads();
+        const bool shared_ok = sm.no_helpers == 0;
+        if (shared_ok && kind == 1) {
+            for (int j = threadIdx.x; j < nch; j += blockDim.x) {
+                sm.fr[j] = __ldcg(job_fr(a, b) + j);
+                sm.sum[j] = __ldcg(job_sums(a, b) + j);
+                if (MODE == A11S_ACCEPT_STOCH_DRAFT) {
+                    sm.qfr[j] = __ldcg(job_qfr(a, b) + j);
+                    sm.qsum[j] = __ldcg(job_qsums(a, b) + j);
+                }
+            }
+        } else if (shared_ok) {
+            for (int j = threadIdx.x; j < nch; j += blockDim.x) sm.tmp[j] = __ldcg(job_sums(a, b) + j);
+        }
+        __syncthreads();
+        return shared_ok;
+    };
     if (warp == 0) {
         int okl = seq_ok ? 1 : 0;
         for (int i = 1 + lane; i < n_live; i += 32)
@@ -647,7 +988,11 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     }
     __syncthreads();
     if (!sm.ok) {
-        if (threadIdx.x == 0) { a.accept_len[b] = 0; a.bonus[b] = -1; }
+        if (threadIdx.x == 0) {
+            a.accept_len[b] = 0;
+            a.bonus[b] = -1;
+            atomicAdd(a.walkers_done, 1);  // helpers leave once every walk has finished
+        }
         return;
     }
 
@@ -660,8 +1005,10 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             if (!has_child) continue;
             const char *prow = tgt_b + (size_t)r * row_bytes;
             const float *rec = r == 0 ? nullptr : records(r);
-            row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, rec, nch, V, a.k,
-                                 sm.fr, sm.sum, warp, lane, a.status, b);
+            const bool rec_q = MODE != A11S_ACCEPT_STOCH_DRAFT || r == 0 || records(N + r) != nullptr;
+            if (!(r != 0 && rec && rec_q && run_pass(1, r)))
+                row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, rec, nch, V,
+                                     a.k, sm.fr, sm.sum, warp, lane, a.status, b);
             __syncthreads();
             if (warp == 0) {
                 const RowStat rs = combine_sums(sm.fr, sm.sum, nch, lane);
@@ -722,10 +1069,14 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
             const float *rec_p = nd == 0 ? nullptr : records(nd);
             const float *rec_q = MODE == A11S_ACCEPT_STOCH_DRAFT && nd != 0 ? records(N + nd) : nullptr;
-            row_stats_into<BF16>(prow, cmax_b, rs_p, rec_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
-            if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, rec_q, nch, V, a.k,
-                                     sm.qfr, sm.qsum, warp, lane, a.status, b);
+            // a recorded non-root row: its statistics shared with the helpers
+            const bool shared = nd != 0 && rec_p && (MODE != A11S_ACCEPT_STOCH_DRAFT || rec_q) && run_pass(1, nd);
+            if (!shared) {
+                row_stats_into<BF16>(prow, cmax_b, rs_p, rec_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
+                if (MODE == A11S_ACCEPT_STOCH_DRAFT)
+                    row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, rec_q, nch, V,
+                                         a.k, sm.qfr, sm.qsum, warp, lane, a.status, b);
+            }
             __syncthreads();
             if (warp == 0) {
                 sm.ps = combine_sums(sm.fr, sm.sum, nch, lane);
@@ -846,35 +1197,18 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                     }
                     if (action == 0) break;
                     if (action == 4) {
-                        // DRAFT residual pass: chunk totals of level L+1 (every warp).
+                        // DRAFT residual pass: chunk totals of level L+1 into sm.tmp,
+                        // shared with the helper blocks (see SharedPass).
                         const int L = sm.L;
-                        constexpr int EPV = Vec<BF16>::EPV, NV = Vec<BF16>::NV, G = 4;
-                        for (int j = warp; j < nch; j += kWarps) {
-                            const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
-                            const int32_t fp = sm.fr[j], fq = sm.qfr[j];
-                            const double scp = chunk_scale(sm.ps, fp), scq = chunk_scale(sm.qs, fq);
-                            uint64_t s = 0;
-                            for (int i0 = 0; i0 < NV; i0 += G) {  // 4 vectors of p and q in flight
-                                uint4 vp[G], vq[G];
-#pragma unroll
-                                for (int g = 0; g < G; ++g) {
-                                    const int e0 = ((i0 + g) * 32 + lane) * EPV;
-                                    const size_t off = (size_t)(c0 + e0) * (BF16 ? 2 : 4);
-                                    const uint32_t ninf = BF16 ? 0xFF80FF80u : 0xFF800000u;
-                                    vp[g] = e0 < clen ? ldg_stream(prow + off) : make_uint4(ninf, ninf, ninf, ninf);
-                                    vq[g] = e0 < clen ? ldg_stream(qrow + off) : make_uint4(ninf, ninf, ninf, ninf);
-                                }
-#pragma unroll
-                                for (int g = 0; g < G; ++g)
-#pragma unroll
-                                    for (int e = 0; e < EPV; ++e) {
-                                        const float pv = prob_of(Vec<BF16>::at(vp[g], e), a.k, fp, scp);
-                                        const float qv = prob_of(Vec<BF16>::at(vq[g], e), a.k, fq, scq);
-                                        s += level_weight(level_prob(pv, qv, L, sm.invT), qv);
-                                    }
+                        const bool local = !run_pass(0, nd);
+                        if (local) {
+                            for (int j = warp; j < nch; j += kWarps) {
+                                const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, V - c0);
+                                const uint64_t sum = resid_chunk_sum<BF16>(prow, qrow, c0, clen, a.k, sm.fr[j], sm.qfr[j],
+                                                                           chunk_scale(sm.ps, sm.fr[j]),
+                                                                           chunk_scale(sm.qs, sm.qfr[j]), L, sm.invT, lane);
+                                if (lane == 0) sm.tmp[j] = sum;
                             }
-                            s = warp_sum_u64(s);
-                            if (lane == 0) sm.tmp[j] = s;
                         }
                         __syncthreads();
                         if (warp == 0) {
@@ -987,21 +1321,29 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     }
     if (failed && warp == 0)
         for (int i = lane; i < N; i += 32) { an[i] = -1; at[i] = -1; }
+    if (threadIdx.x == 0) atomicAdd(a.walkers_done, 1);  // helpers leave once every walk has finished
 }
 
 // Before every acceptance launch: clear the status word and set every record
 // to kUnrecorded (one launch instead of two memsets).
-__global__ void accept_init_kernel(StatusWord *st, uint4 *recs, size_t n16) {
+__global__ void accept_init_kernel(StatusWord *st, uint4 *recs, size_t n16, uint4 *zero, size_t z16) {
     const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if (i0 == 0) *st = StatusWord{};
+    if (i0 == 0) {
+        *st = StatusWord{};
+        reinterpret_cast<uint4 *>(st)[1] = make_uint4(0, 0, 0, 0);  // the finished-walk counter at byte 16
+    }
     const uint4 u = make_uint4(kUnrecorded, kUnrecorded, kUnrecorded, kUnrecorded);
     for (size_t i = i0; i < n16; i += (size_t)gridDim.x * blockDim.x) recs[i] = u;
+    for (size_t i = i0; i < z16; i += (size_t)gridDim.x * blockDim.x) zero[i] = make_uint4(0, 0, 0, 0);
 }
 
-cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, cudaStream_t s) {
-    const size_t n16 = bytes / 16;
-    const unsigned blocks = (unsigned)std::min<size_t>((n16 + 255) / 256, 4 * 148);
-    accept_init_kernel<<<blocks ? blocks : 1, 256, 0, s>>>(st, reinterpret_cast<uint4 *>(recs), n16);
+cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, void *zero, size_t zero_bytes,
+                               cudaStream_t s) {
+    const size_t n16 = bytes / 16, z16 = zero ? zero_bytes / 16 : 0;
+    const size_t n = std::max(n16, z16);
+    const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 4 * 148);
+    accept_init_kernel<<<blocks ? blocks : 1, 256, 0, s>>>(st, reinterpret_cast<uint4 *>(recs), n16,
+                                                           reinterpret_cast<uint4 *>(zero), z16);
     return cudaGetLastError();
 }
 

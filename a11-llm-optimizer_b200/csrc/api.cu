@@ -53,7 +53,7 @@ int sm_count() {
 // each launch) | weight sums of the root rows [B][2][nch] uint64 (sampling
 // modes); rows = max_nodes, or 2 max_nodes in DRAFT (p rows, then q rows)
 struct AcceptLayout {
-    size_t recs, arg, root_sums, total;
+    size_t recs, arg, root_sums, jobs, total;
 };
 AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32_t vocab) {
     AcceptLayout L;
@@ -62,7 +62,8 @@ AcceptLayout accept_layout(int32_t mode, int32_t batch, int32_t max_nodes, int32
     L.recs = kHeaderBytes;
     L.arg = L.recs + up256(rows * nch * sizeof(float));
     L.root_sums = L.arg + (mode == A11S_ACCEPT_GREEDY ? up256(rows * nch * sizeof(int32_t)) : 0);
-    L.total = L.root_sums + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * 2 * nch * sizeof(uint64_t)));
+    L.jobs = L.root_sums + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * 2 * nch * sizeof(uint64_t)));
+    L.total = L.jobs + (mode == A11S_ACCEPT_GREEDY ? 0 : up256((size_t)batch * a11s::accept_job_bytes((int)nch)));
     return L;
 }
 
@@ -170,6 +171,9 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.recs = reinterpret_cast<float *>(ws + L.recs);
     a.arg = mode == A11S_ACCEPT_GREEDY ? reinterpret_cast<int32_t *>(ws + L.arg) : nullptr;
     a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
+    a.walkers_done = reinterpret_cast<int32_t *>(ws + 16);  // header: status word at 0, counter at 16
+    a.jobs = mode == A11S_ACCEPT_GREEDY ? nullptr : ws + L.jobs;
+    a.job_stride = (int64_t)a11s::accept_job_bytes(a.nch);
     // A walking block may wait for rows that other blocks record only when the
     // walkers (one block per sequence, the first ones scheduled) fill at most
     // half of the 2 resident blocks per SM: the bulk pass always has room.
@@ -187,10 +191,18 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     if (slice < 16) slice = 16;
     if (slice > rest && rest > 0) slice = rest;
     a.slice = (int32_t)slice;
-    const int grid_y = 1 + (int)((rest + slice - 1) / slice);
+    int grid_y = 1 + (int)((rest + slice - 1) / slice);
+    a.bulk_rows = grid_y;
+    if (mode != A11S_ACCEPT_GREEDY) {
+        // Helper rows: blocks scheduled after every walking and streaming block
+        // that take chunks of the walks' row passes, about two per SM.
+        const int helper_rows = (2 * sm_count() + batch - 1) / batch;
+        grid_y += helper_rows < 1 ? 1 : helper_rows;
+    }
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = a11s::launch_accept_init(a.status, ws + L.recs, L.root_sums - L.recs, s);
+    cudaError_t e = a11s::launch_accept_init(a.status, ws + L.recs, L.root_sums - L.recs, a.jobs,
+                                             a.jobs ? L.total - L.jobs : 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: clearing workspace");
     e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_y, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: launch");

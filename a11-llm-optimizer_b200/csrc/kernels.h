@@ -31,11 +31,23 @@ struct AcceptArgs {
                            // resident with at least as many slots left for the bulk pass
     unsigned long long *root_sums;  // [B][2][nch] weight sums of the root rows (p, q)
     StatusWord *status;
+    // Row passes of the sampling walks shared with helper blocks (null in GREEDY):
+    // per sequence a job of job_stride bytes (SharedPass, then int32 frames fr[nch],
+    // qfr[nch] and uint64 chunk sums[nch], qsums[nch]); walkers_done counts finished walks.
+    char *jobs;
+    int64_t job_stride;
+    int32_t *walkers_done;
+    int32_t bulk_rows;  // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
 };
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s);
-// Clears the status word and marks every record unwritten (bytes: a multiple of 16).
-cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, cudaStream_t s);
+// Clears the status word and the 16 bytes after it, marks every record unwritten
+// (bytes: a multiple of 16) and zeroes `zero_bytes` at `zero` (a multiple of 16;
+// nullable).
+cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, void *zero, size_t zero_bytes,
+                               cudaStream_t s);
+// Bytes of one sequence's shared-pass area (sampling modes).
+size_t accept_job_bytes(int nch);
 
 struct CompactArgs {
     char *k_pool;

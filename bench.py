@@ -326,34 +326,11 @@ def run_ours(args, rank, world, local_rank):
     grown = torch.empty(B, dtype=torch.int32, device=dev)
     ev_kernels = []  # per timed step: (attention start, end, accept start, end)
 
-    # Acceptance counters: K3 accumulates them on the device every step. Every
+    # Acceptance counters: K3 accumulates them on the device every step; every
     # REDUCE_EVERY steps a snapshot is all-reduced over the ranks on a side
-    # stream, so the collective overlaps the next steps' kernels instead of
-    # sitting on the compute stream; two snapshot buffers alternate, and a
-    # buffer is rewritten only after the all-reduce that last read it.
-    side = torch.cuda.Stream(device=dev) if world > 1 else None
-    snaps = [torch.zeros_like(stats) for _ in range(2)]
-    snap_read = [torch.cuda.Event(), torch.cuda.Event()]
-    snap_taken = torch.cuda.Event()
-    reduce_state = {"steps": 0, "reduces": 0, "last": None}
-
-    def reduce_counters():
-        k = reduce_state["steps"]
-        reduce_state["steps"] += 1
-        if side is None or k % REDUCE_EVERY != REDUCE_EVERY - 1:
-            return
-        j = reduce_state["reduces"] % 2
-        cur = torch.cuda.current_stream()
-        if reduce_state["reduces"] >= 2:
-            cur.wait_event(snap_read[j])
-        snaps[j].copy_(stats)
-        snap_taken.record(cur)
-        side.wait_event(snap_taken)
-        with torch.cuda.stream(side):
-            torch.distributed.all_reduce(snaps[j], op=torch.distributed.ReduceOp.SUM)
-            snap_read[j].record(side)
-        reduce_state["reduces"] += 1
-        reduce_state["last"] = (j, reduce_state["steps"])
+    # stream, overlapping the next steps' kernels (a11spec.distributed.CounterReducer).
+    from a11spec.distributed import CounterReducer
+    reducer = CounterReducer(stats, every=REDUCE_EVERY)
 
     def step(timed_events=None, inputs=None, ready=None, out_free=None):
         # inputs: (hidden, q, last, uniforms) of this step; default the resident
@@ -401,7 +378,7 @@ def run_ours(args, rank, world, local_rank):
         pages.release(freed, n_freed)
         # next root pair: (last accepted token or old root, bonus)
         a11spec.next_roots(tk, acc.accepted_tokens, acc.accept_len, acc.bonus, lst)
-        reduce_counters()
+        reducer.step()
 
     def barrier():
         if world > 1:
@@ -494,9 +471,8 @@ def run_ours(args, rank, world, local_rank):
     e2e_ms = x0.elapsed_time(x1)
     e2e_emitted = int((stats - s1)[STAT_NAMES.index("emitted_tokens")])
 
-    if side is not None:
-        torch.cuda.current_stream().wait_stream(side)
-        torch.cuda.synchronize()
+    reducer.finish()
+    torch.cuda.synchronize()
     t = torch.tensor([ms, e2e_ms, attn_ms, acc_ms], dtype=torch.float64, device=dev)
     cnt = torch.tensor([emitted, e2e_emitted], dtype=torch.int64, device=dev)
     if world > 1:
@@ -533,10 +509,8 @@ def run_ours(args, rank, world, local_rank):
         "gpu_launches": args.steps * launches_per_step,
         "clocks": clk.summary(),
     }
-    if reduce_state["last"] is not None:
-        j, through = reduce_state["last"]
-        line["acceptance_stats_global"] = dict(zip(STAT_NAMES, (int(x) for x in snaps[j].tolist())),
-                                               through_step=through, ranks=world)
+    if reducer.result() is not None:
+        line["acceptance_stats_global"] = reducer.result()
     if world == 1 and not args.no_configs:
         line["configs"] = measure_configs(dev, pk)
     if host_copy is not None:

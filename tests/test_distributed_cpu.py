@@ -32,6 +32,18 @@ def _worker(rank, world, port, mode, q):
             tot = D.reduce_stats(stats)
             t = D.max_time(10.0 + rank)
             q.put((rank, tot.tolist(), t, stats.tolist()))
+        elif mode == "periodic":
+            # the bench's counter reduction: every 5 steps, 12 steps -> after steps 5 and 10
+            stats = torch.zeros(6, dtype=torch.int64)
+            red = D.CounterReducer(stats, every=5)
+            seen = []
+            for _ in range(12):
+                stats += torch.arange(6, dtype=torch.int64) + rank  # this step's counters
+                red.step()
+                if red.result() is not None:
+                    seen.append(red.result()["through_step"])
+            red.finish()
+            q.put((rank, red.result(), sorted(set(seen)), red.reduces))
         else:
             if rank == 1:
                 raise RuntimeError("rank 1 fails before the step's collective")
@@ -76,6 +88,19 @@ def test_counters_sum_and_time_max_over_ranks():
         tot, t, local = out[r]
         assert tot == expect and t == 11.0
         assert local == [i * (r + 1) for i in range(6)]  # reduce_stats leaves its input alone
+
+
+def test_periodic_counter_reduction():
+    """CounterReducer (the bench's multi-GPU counter sum) all-reduces a snapshot
+    every 5 steps; both ranks see the same sums, covering steps 1-10 of 12."""
+    out = _run("periodic")
+    want = [10 * (2 * i + 1) for i in range(6)]  # 10 steps of (i + 0) + (i + 1)
+    for r in range(2):
+        res, seen, reduces = out[r]
+        assert reduces == 2 and seen == [5, 10]
+        assert res["through_step"] == 10 and res["ranks"] == 2
+        from a11spec._lib import STAT_NAMES
+        assert [res[n] for n in STAT_NAMES] == want
 
 
 def test_failed_rank_ends_peer_collective_with_error():
