@@ -602,63 +602,73 @@ __device__ void pass_chunk(const AcceptArgs &a, int b, int kind, int node, int L
     }
 }
 
-// Helper blocks (grid rows >= bulk_rows, sampling modes): thread 0 looks for
-// an open pass with unclaimed chunks, starting at a sequence of its own, and
-// claims one chunk per warp; each warp computes its chunk. The block leaves
-// once every walk has finished (or its budget ran out). A pass's parameters
-// were written before it was opened; they are read from L2 after the claim.
+// Take chunks of the walks' open passes, one warp at a time (sampling modes).
+// Lane 0 looks for an open pass with an unclaimed chunk, starting at a
+// sequence of its own, and claims one chunk; the warp computes it. A pass's
+// parameters were written before it was opened; they are read from L2 after
+// the claim. Helper blocks (grid rows >= bulk_rows) keep looking until every
+// walk has finished (or their budget ran out); a streaming block that has
+// finished its own units leaves as soon as a scan finds nothing open.
 template <int MODE, bool BF16>
-__device__ void pass_helper(const AcceptArgs &a, int warp, int lane) {
-    __shared__ double s_invT[A11S_MAX_WALK_LEVELS + 1];
-    __shared__ int s_b, s_j0, s_n;
+__device__ void help_passes(const AcceptArgs &a, int warp, int lane, bool until_walks_end, double *invT) {
     const long long t0 = clock64();
-    int start = (int)(blockIdx.x + (blockIdx.y - a.bulk_rows) * gridDim.x) % a.B;
+    int start = (int)((blockIdx.y * gridDim.x + blockIdx.x) * kWarps + warp) % a.B;
     for (;;) {
-        if (threadIdx.x == 0) {
-            int b = -1, j0 = -1, n = 0;
-            if (ld_relaxed(a.walkers_done) >= (uint32_t)a.B || clock64() - t0 > kHelperBudget) {
-                b = -2;
-            } else {
-                for (int t = 0; t < a.B && n == 0; ++t) {
-                    const int bb = (start + t) % a.B;
-                    SharedPass *job = job_of(a, bb);
-                    const unsigned long long w = ld_relaxed_u64(&job->word);
-                    const uint32_t g = (uint32_t)(w >> 32);
-                    if (g == 0) continue;
-                    j0 = claim_chunks(&job->word, g, a.nch, kWarps, &n);
-                    if (n) b = bb;
+        int b = -1, j = -1;
+        bool leave = false;
+        if (until_walks_end) {
+            leave = ld_relaxed(a.walkers_done) >= (uint32_t)a.B || clock64() - t0 > kHelperBudget;
+        } else {
+            leave = ld_relaxed(a.open_passes) == 0;  // one load: nothing open, a streaming block leaves
+        }
+        leave = __shfl_sync(0xffffffffu, leave, 0);
+        if (leave) return;
+        // the lanes read 32 sequences' pass words at once; lane 0 claims from
+        // the first open pass with a chunk left
+        for (int t0s = 0; t0s < a.B && j < 0; t0s += 32) {
+            const int bb = (start + t0s + lane) % a.B;
+            unsigned long long w = 0;
+            if (t0s + lane < a.B) w = ld_relaxed_u64(&job_of(a, bb)->word);
+            const uint32_t g = (uint32_t)(w >> 32);
+            const unsigned open = __ballot_sync(0xffffffffu, g != 0 && (uint32_t)w < (uint32_t)a.nch);
+            for (unsigned m = open; m && j < 0; m &= m - 1) {
+                const int src = __ffs(m) - 1;
+                const int cb = __shfl_sync(0xffffffffu, bb, src);
+                const uint32_t cg = __shfl_sync(0xffffffffu, g, src);
+                int jj = -1;
+                if (lane == 0) {
+                    int n = 0;
+                    jj = claim_chunks(&job_of(a, cb)->word, cg, a.nch, 1, &n);
+                    if (!n) jj = -1;
+                }
+                jj = __shfl_sync(0xffffffffu, jj, 0);
+                if (jj >= 0) {
+                    b = cb;
+                    j = jj;
                 }
             }
-            s_b = b;
-            s_j0 = j0;
-            s_n = n;
-            if (b >= 0) start = b;  // stay with this pass while it has chunks
         }
-        __syncthreads();
-        const int b = s_b, j0 = s_j0, n = s_n;
-        if (b == -2) return;
-        if (n == 0) {
-            __syncthreads();
-            if (threadIdx.x == 0) __nanosleep(512);
+        if (j < 0) {
+            if (!until_walks_end) return;  // a streaming block does not wait for passes
+            __nanosleep(256);
             continue;
         }
+        start = b;  // stay with this pass while it has chunks
         __threadfence();
         SharedPass *job = job_of(a, b);
         const int kind = __ldcg(&job->kind), node = __ldcg(&job->node), L = __ldcg(&job->L);
         if (kind == 0)
-            for (int l = threadIdx.x; l <= L; l += blockDim.x) s_invT[l] = __ldcg(&job->invT[l]);
-        __syncthreads();
-        if (warp < n) {
-            RowStat ps, qs;
-            ps.C = __ldcg(&job->ps.C);
-            ps.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->ps.S));
-            ps.invS = __ldcg(&job->ps.invS);
-            qs.C = __ldcg(&job->qs.C);
-            qs.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->qs.S));
-            qs.invS = __ldcg(&job->qs.invS);
-            pass_chunk<MODE, BF16>(a, b, kind, node, L, ps, qs, s_invT, j0 + warp, lane);
-        }
-        __syncthreads();  // s_invT and the claim are reused
+            for (int l = lane; l <= L; l += 32) invT[l] = __ldcg(&job->invT[l]);
+        __syncwarp();
+        RowStat ps, qs;
+        ps.C = __ldcg(&job->ps.C);
+        ps.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->ps.S));
+        ps.invS = __ldcg(&job->ps.invS);
+        qs.C = __ldcg(&job->qs.C);
+        qs.S = __ldcg(reinterpret_cast<const unsigned long long *>(&job->qs.S));
+        qs.invS = __ldcg(&job->qs.invS);
+        pass_chunk<MODE, BF16>(a, b, kind, node, L, ps, qs, invT, j, lane);
+        __syncwarp();  // invT is rewritten by the next claim
     }
 }
 
@@ -797,8 +807,9 @@ __device__ int row_argmax_rec(const float *cmax, const int32_t *arg, int nch, in
 template <int MODE, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    __shared__ double s_invT[MODE == A11S_ACCEPT_GREEDY ? 1 : kWarps][A11S_MAX_WALK_LEVELS + 1];
     if ((int)blockIdx.y >= a.bulk_rows) {  // helper block (sampling modes only)
-        if constexpr (MODE != A11S_ACCEPT_GREEDY) pass_helper<MODE, BF16>(a, warp, lane);
+        if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, true, s_invT[warp]);
         return;
     }
     int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
@@ -810,13 +821,24 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // Units of a sequence: first the root rows' chunks (the p root, and the q
     // root in DRAFT mode), then the other rows in index order (p rows 1..N-1,
     // then q rows 1..N-1), a row's chunks consecutive, so the rows near the
-    // root, which the walk visits first, are recorded first. Slice 0 is
-    // exactly the root units; its block then walks the tree while the bulk
-    // pass goes on in other blocks.
+    // root, which the walk visits first, are recorded first. Grid row 0 is the
+    // sequence's walker; in the sampling modes it streams nothing and rows 1 ..
+    // root_blocks take the root units (chunk maxima and weight sums), one per
+    // warp, so every root is recorded in the first wave by many SMs at once;
+    // in GREEDY the walker records its root itself (root_blocks = 0). The rows
+    // after them take the other units in slices.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
-    const int u0 = blockIdx.y == 0 ? 0 : n_root_units + (blockIdx.y - 1) * a.slice;
-    const int u1 = blockIdx.y == 0 ? n_root_units : min(u0 + a.slice, a.units_per_seq);
+    int u0 = 0, u1 = 0;
+    if (blockIdx.y == 0 && a.root_blocks == 0) {
+        u1 = n_root_units;  // GREEDY: the walker records its root itself (maxima only, cheap)
+    } else if (blockIdx.y >= 1 && (int)blockIdx.y <= a.root_blocks) {
+        u0 = (blockIdx.y - 1) * kWarps;
+        u1 = min(u0 + kWarps, n_root_units);
+    } else if ((int)blockIdx.y > a.root_blocks) {
+        u0 = n_root_units + (blockIdx.y - 1 - a.root_blocks) * a.slice;
+        u1 = min(u0 + a.slice, a.units_per_seq);
+    }
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += kWarps) {
         int j, r;
@@ -840,21 +862,28 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
         const size_t rrow = (size_t)b * a.rows_per_seq + r;
-        if (lane == 0) {  // each record is written once, over the launch's sentinel
-            st_relaxed(a.recs + rrow * a.nch + j, __float_as_uint(m));
-            if (MODE == A11S_ACCEPT_GREEDY) st_relaxed(a.arg + rrow * a.nch + j, (uint32_t)first);
-        }
         if (MODE != A11S_ACCEPT_GREEDY && node == 0) {
             // The walk always starts at the root: its weight sums are taken
-            // here, while the chunk is hot in L2, instead of in the walk.
+            // here, while the chunk is hot in L2, and stored before the
+            // chunk's record, which tells the walker they are there.
             const int32_t f = m < INFINITY ? frame_of(m, a.k) : A11S_FRAME_NONE;
             const uint64_t s = f == A11S_FRAME_NONE ? 0ull : chunk_wsum<BF16>(row, c0, clen, a.k, (float)f, lane);
-            if (lane == 0) a.root_sums[((size_t)b * 2 + (isq ? 1 : 0)) * a.nch + j] = s;
+            if (lane == 0) {
+                __stcg(a.root_sums + ((size_t)b * 2 + (isq ? 1 : 0)) * a.nch + j, (unsigned long long)s);
+                __threadfence();
+            }
+        }
+        if (lane == 0) {  // each record is written once, over the launch's sentinel
+            if (MODE == A11S_ACCEPT_GREEDY) st_relaxed(a.arg + rrow * a.nch + j, (uint32_t)first);
+            st_relaxed(a.recs + rrow * a.nch + j, __float_as_uint(m));
         }
     }
     if (warp_or(bad) && lane == 0) report(a.status, A11S_ENONFINITE, b);
-    if (blockIdx.y != 0) return;
-    __syncthreads();  // the root rows' records and weight sums were written by this block
+    if (blockIdx.y != 0) {
+        // a streaming block that is done takes chunks of open walk passes before it leaves
+        if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, false, s_invT[warp]);
+        return;
+    }
 
     // ---------------- phase 2: walk ----------------
     __shared__ WalkSmem sm;
@@ -878,6 +907,9 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                 sm.cmx[threadIdx.x] = __uint_as_float(v);
                 sm.carg[threadIdx.x] = (int32_t)pv;
             }
+            // a root chunk's weight sum was stored before its record: this
+            // thread reads it after the record (row_stats_into, chunk j = thread j)
+            __threadfence();
         }
         return __syncthreads_and(mine) ? rec : nullptr;
     };
@@ -922,25 +954,25 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         __syncthreads();
         if (threadIdx.x == 0) {
             sm.gen += 1;
+            atomicAdd(a.open_passes, 1);  // streaming blocks that finish look for open passes
             atomicExch(&job->word, (unsigned long long)sm.gen << 32);  // open the pass
         }
         __syncthreads();
         const uint32_t gen = sm.gen;
         const int L = sm.L;
         const RowStat ps = sm.ps, qs = sm.qs;
-        for (;;) {  // this block takes chunks too, one per warp
-            if (threadIdx.x == 0) {
+        for (;;) {  // this block takes chunks too, one warp at a time
+            int j = -1;
+            if (lane == 0) {
                 int n = 0;
-                const int j0 = claim_chunks(&job->word, gen, nch, kWarps, &n);
-                sm.res[0] = j0;
-                sm.res[1] = n;
+                j = claim_chunks(&job->word, gen, nch, 1, &n);
+                if (!n) j = -1;
             }
-            __syncthreads();
-            const int j0 = sm.res[0], n = sm.res[1];
-            __syncthreads();  // sm.res is read by every thread before it changes
-            if (n == 0) break;
-            if (warp < n) pass_chunk<MODE, BF16>(a, b, kind, nd, L, ps, qs, sm.invT, j0 + warp, lane);
+            j = __shfl_sync(0xffffffffu, j, 0);
+            if (j < 0) break;
+            pass_chunk<MODE, BF16>(a, b, kind, nd, L, ps, qs, sm.invT, j, lane);
         }
+        __syncthreads();
         if (threadIdx.x == 0) {  // the helpers' last chunks (bounded wait)
             const long long t0 = clock64();
             bool all = false;
@@ -954,6 +986,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                 atomicExch(&job->word, ((unsigned long long)gen << 32) | 0xFFFFFFFFull);
                 sm.no_helpers = 1;
             }
+            atomicSub(a.open_passes, 1);
             __threadfence();
         }
         __syncthreads();
@@ -1004,11 +1037,14 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             for (int c = r + 1; c < n_live && !has_child; ++c) has_child = sm.par[c] == r;
             if (!has_child) continue;
             const char *prow = tgt_b + (size_t)r * row_bytes;
-            const float *rec = r == 0 ? nullptr : records(r);
-            const bool rec_q = MODE != A11S_ACCEPT_STOCH_DRAFT || r == 0 || records(N + r) != nullptr;
-            if (!(r != 0 && rec && rec_q && run_pass(1, r)))
-                row_stats_into<BF16>(prow, cmax_b, r == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr, rec, nch, V,
-                                     a.k, sm.fr, sm.sum, warp, lane, a.status, b);
+            const float *rec = records(r);
+            const bool rec_q = MODE != A11S_ACCEPT_STOCH_DRAFT || records(N + r) != nullptr;
+            if (!(r != 0 && rec && rec_q && run_pass(1, r))) {
+                // the root's sums come from the bulk pass once its records are in
+                const unsigned long long *rs = r == 0 && rec ? a.root_sums + (size_t)b * 2 * nch : nullptr;
+                row_stats_into<BF16>(prow, cmax_b, rs, rs ? nullptr : rec, nch, V, a.k, sm.fr, sm.sum, warp, lane,
+                                     a.status, b);
+            }
             __syncthreads();
             if (warp == 0) {
                 const RowStat rs = combine_sums(sm.fr, sm.sum, nch, lane);
@@ -1064,18 +1100,21 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         __syncthreads();
         for (;;) {  // one iteration per visited node
             const int nd = sm.node;
-            const unsigned long long *rs_p = nd == 0 ? a.root_sums + (size_t)b * 2 * nch : nullptr;
             const char *prow = tgt_b + (size_t)nd * row_bytes;
             const char *qrow = MODE == A11S_ACCEPT_STOCH_DRAFT ? drf_b + (size_t)nd * row_bytes : nullptr;
-            const float *rec_p = nd == 0 ? nullptr : records(nd);
-            const float *rec_q = MODE == A11S_ACCEPT_STOCH_DRAFT && nd != 0 ? records(N + nd) : nullptr;
-            // a recorded non-root row: its statistics shared with the helpers
-            const bool shared = nd != 0 && rec_p && (MODE != A11S_ACCEPT_STOCH_DRAFT || rec_q) && run_pass(1, nd);
+            const float *rec_p = records(nd);
+            const float *rec_q = MODE == A11S_ACCEPT_STOCH_DRAFT ? records(N + nd) : nullptr;
+            const bool have = rec_p && (MODE != A11S_ACCEPT_STOCH_DRAFT || rec_q);
+            // a recorded non-root row: its statistics shared with the helpers;
+            // the root's come from the bulk pass once its records are in
+            const bool shared = nd != 0 && have && run_pass(1, nd);
             if (!shared) {
-                row_stats_into<BF16>(prow, cmax_b, rs_p, rec_p, nch, V, a.k, sm.fr, sm.sum, warp, lane, a.status, b);
+                const unsigned long long *rs_p = nd == 0 && have ? a.root_sums + (size_t)b * 2 * nch : nullptr;
+                row_stats_into<BF16>(prow, cmax_b, rs_p, rs_p ? nullptr : rec_p, nch, V, a.k, sm.fr, sm.sum, warp, lane,
+                                     a.status, b);
                 if (MODE == A11S_ACCEPT_STOCH_DRAFT)
-                    row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, nd == 0 ? rs_p + nch : nullptr, rec_q, nch, V,
-                                         a.k, sm.qfr, sm.qsum, warp, lane, a.status, b);
+                    row_stats_into<BF16>(qrow, cmax_b + (size_t)N * nch, rs_p ? rs_p + nch : nullptr,
+                                         rs_p ? nullptr : rec_q, nch, V, a.k, sm.qfr, sm.qsum, warp, lane, a.status, b);
             }
             __syncthreads();
             if (warp == 0) {

@@ -171,7 +171,8 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.recs = reinterpret_cast<float *>(ws + L.recs);
     a.arg = mode == A11S_ACCEPT_GREEDY ? reinterpret_cast<int32_t *>(ws + L.arg) : nullptr;
     a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
-    a.walkers_done = reinterpret_cast<int32_t *>(ws + 16);  // header: status word at 0, counter at 16
+    a.walkers_done = reinterpret_cast<int32_t *>(ws + 16);  // header: status word at 0, counters at 16 and 20
+    a.open_passes = reinterpret_cast<int32_t *>(ws + 20);
     a.jobs = mode == A11S_ACCEPT_GREEDY ? nullptr : ws + L.jobs;
     a.job_stride = (int64_t)a11s::accept_job_bytes(a.nch);
     // A walking block may wait for rows that other blocks record only when the
@@ -179,11 +180,14 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     // half of the 2 resident blocks per SM: the bulk pass always has room.
     a.wait_records = batch <= sm_count() ? 1 : 0;
 
-    // Slice 0 of a sequence is exactly its root rows' units, so that block
-    // reads only the root rows before it walks the tree. The other units are
-    // balanced: about 4 waves of 2 resident 512-thread blocks per SM, at least
-    // 16 chunks (one per warp) per block.
+    // Grid row 0 of a sequence walks its tree; in the sampling modes it streams
+    // nothing and rows 1 .. root_blocks take its root rows' units (maxima and
+    // weight sums), one per warp, so every root is recorded in the first wave;
+    // in GREEDY the walker records its root itself. The other units are balanced over about 4
+    // waves of 2 resident 512-thread blocks per SM, at least 16 chunks (one
+    // per warp) per block.
     const int root_units = a.nch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
+    a.root_blocks = mode == A11S_ACCEPT_GREEDY ? 0 : (root_units + 15) / 16;
     const long long rest = (long long)a.units_per_seq - root_units;
     const long long target_blocks = (long long)sm_count() * 2 * 4;
     long long slice = ((long long)batch * rest + target_blocks - 1) / target_blocks;
@@ -191,7 +195,7 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     if (slice < 16) slice = 16;
     if (slice > rest && rest > 0) slice = rest;
     a.slice = (int32_t)slice;
-    int grid_y = 1 + (int)((rest + slice - 1) / slice);
+    int grid_y = 1 + a.root_blocks + (int)((rest + slice - 1) / slice);
     a.bulk_rows = grid_y;
     if (mode != A11S_ACCEPT_GREEDY) {
         // Helper rows: blocks scheduled after every walking and streaming block

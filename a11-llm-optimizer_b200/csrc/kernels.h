@@ -37,7 +37,9 @@ struct AcceptArgs {
     char *jobs;
     int64_t job_stride;
     int32_t *walkers_done;
-    int32_t bulk_rows;  // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
+    int32_t *open_passes;  // passes published and not yet complete
+    int32_t bulk_rows;    // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
+    int32_t root_blocks;  // grid rows 1 .. root_blocks take the root units, one per warp (0: the walker does)
 };
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s);

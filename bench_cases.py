@@ -71,11 +71,18 @@ def case_attention(a) -> dict:
 
 
 def case_accept(a) -> dict:
-    """Acceptance over bf16 logits [batch, 64, 151936] (greedy / one-hot) or
+    """Acceptance over bf16 logits [batch, 64, 151936] (greedy / one-hot, random
+    drafts: walks stop at the root), the C4 greedy case (make_c4: random trees,
+    50 % of the drafts forced to their parent's argmax, so walks go deep) or
     fp32 p and q [batch, 63, 151936] (draft mode, C3 shape)."""
     dev = "cuda"
     g = torch.Generator(device=dev).manual_seed(5)
-    if a.mode == "draft":
+    if a.mode == "c4greedy":
+        d = W.make_c4(seed=4, batch=a.batch, device=dev)
+        args = (a11spec.GREEDY, d["logits"], d["tokens"], d["parents"], d["n_nodes"])
+        kw = {}
+        nbytes = d["logits"].numel() * 2.0
+    elif a.mode == "draft":
         d = W.make_c3(seed=3, batch=a.batch, device=dev)
         args = (2, d["p"], d["tokens"], d["parents"], d["n_nodes"])
         kw = dict(draft_logits=d["q"], temperature=0.8, uniforms=d["uniforms"])
@@ -193,7 +200,7 @@ def main(argv=None) -> None:
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--nodes", type=int, default=64)
-    ap.add_argument("--mode", choices=["greedy", "onehot", "draft"], default="greedy")
+    ap.add_argument("--mode", choices=["greedy", "onehot", "draft", "c4greedy"], default="greedy")
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--iters", type=int, default=2)
     a = ap.parse_args(argv)
