@@ -819,8 +819,8 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
 
     // ---------------- phase 1: chunk maxima ----------------
     // Units of a sequence: first the root rows' chunks (the p root, and the q
-    // root in DRAFT mode), then the other rows in index order (p rows 1..N-1,
-    // then q rows 1..N-1), a row's chunks consecutive, so the rows near the
+    // root in DRAFT mode), then the other rows in index order (in DRAFT mode
+    // p row i then q row i), a row's chunks consecutive, so the rows near the
     // root, which the walk visits first, are recorded first. Grid row 0 is the
     // sequence's walker; in the sampling modes it streams nothing and rows 1 ..
     // root_blocks take the root units (chunk maxima and weight sums), one per
@@ -846,10 +846,12 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             j = u / kRootRows;
             r = (u - j * kRootRows) ? a.N : 0;
         } else {
+            // rows 1..N-1 in index order, in STOCH_DRAFT each p row followed by
+            // its q row (a visited node needs both)
             const int v = u - n_root_units;
-            const int q = v / a.nch;  // 0..N-2: p rows 1..N-1, then q rows N+1..2N-1
+            const int q = v / a.nch;
             j = v - q * a.nch;
-            r = q < a.N - 1 ? 1 + q : a.N + 1 + (q - (a.N - 1));
+            r = kRootRows == 2 ? ((q & 1) ? a.N + 1 + (q >> 1) : 1 + (q >> 1)) : 1 + q;
         }
         const bool isq = r >= a.N;
         const int node = isq ? r - a.N : r;
@@ -909,7 +911,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             }
             // a root chunk's weight sum was stored before its record: this
             // thread reads it after the record (row_stats_into, chunk j = thread j)
-            __threadfence();
+            if (MODE != A11S_ACCEPT_GREEDY && (r == 0 || r == N)) __threadfence();
         }
         return __syncthreads_and(mine) ? rec : nullptr;
     };
