@@ -57,7 +57,7 @@ def build_ref(ref_root: str | None = None) -> bool:
     # machine without the reference tree can run them against a11_optimizer.
     import py_compile
     py_compile.compile(os.path.join(ref_root, "tests", "test_python_bindings.py"),
-                       cfile=os.path.join(HERE, "_ref", "test_python_bindings.pyc"), doraise=True)
+                       cfile=os.path.join(HERE, "_ref", "test_python_bindings.bytecode"), doraise=True)
     return True
 
 

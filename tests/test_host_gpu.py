@@ -164,7 +164,7 @@ def test_reference_python_binding_tests_against_a11_optimizer(dev):
     import importlib.util
 
     import a11_optimizer
-    pyc = os.path.join(ROOT, "oracle", "_ref", "test_python_bindings.pyc")
+    pyc = os.path.join(ROOT, "oracle", "_ref", "test_python_bindings.bytecode")
     if not os.path.exists(pyc):
         pytest.skip("reference binding tests not compiled (needs the reference tree at build time)")
     loader = importlib.machinery.SourcelessFileLoader("ref_test_python_bindings", pyc)
