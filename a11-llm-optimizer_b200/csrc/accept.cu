@@ -511,11 +511,10 @@ __device__ uint64_t resid_chunk_sum(const char *prow, const char *qrow, int c0, 
 //          in STOCH_DRAFT the q row (qfr, qsums).
 // The walking block publishes the pass (kind, visited node, level L, row
 // statistics, frames, invT) and opens it by writing `word` = (generation << 32)
-// | 0. A block (the walker or a helper) takes chunks for its warps by adding
-// their number to `word` (one atomic per claim); the value the add returns
-// names the pass and the first chunk taken, so a claim never takes a chunk of
-// another pass. Each warp computes its chunk, stores the results and counts
-// the chunk in `done`. The walker publishes the next pass only after `done`
+// | 0. A warp (of the walker or a helper) takes the next chunk by a
+// compare-and-swap of `word` from (generation, j) to (generation, j + 1), so a
+// claim never takes a chunk of another pass. Each warp computes its chunk,
+// stores the results and counts the chunk in `done`. The walker publishes the next pass only after `done`
 // reached the chunk count of the last, so no late write lands in a newer pass.
 // The walker claims chunks too, so a pass finishes even when no helper runs.
 struct SharedPass {
@@ -543,19 +542,25 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const void *p) {
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Claim up to `want` chunks of pass `gen` (one thread): returns the first
-// chunk and sets *count (0 when every chunk is taken or the pass is no longer
-// the open one). An add that finds the pass exhausted only raises its claimed
-// count past the chunk count, which changes nothing.
+// Claim the next chunk of pass `gen` (one thread): returns it and sets
+// *count to 1, or sets *count to 0 when every chunk of the pass is taken or
+// the pass is no longer the open one. A compare-and-swap that names the
+// generation, so a claim can never advance a newer pass's count (a helper
+// that read an older word while the walker reopened the slot fails instead).
 __device__ int claim_chunks(unsigned long long *word, uint32_t gen, int nch, int want, int *count) {
+    (void)want;
     *count = 0;
-    const unsigned long long w = ld_relaxed_u64(word);
-    if ((uint32_t)(w >> 32) != gen || (uint32_t)w >= (uint32_t)nch) return -1;
-    const unsigned long long old = atomicAdd(word, (unsigned long long)want);
-    if ((uint32_t)(old >> 32) != gen || (uint32_t)old >= (uint32_t)nch) return -1;
-    const int j0 = (int)(uint32_t)old;
-    *count = min(want, nch - j0);
-    return j0;
+    unsigned long long w = ld_relaxed_u64(word);
+    for (int tries = 0; tries < 256; ++tries) {
+        if ((uint32_t)(w >> 32) != gen || (uint32_t)w >= (uint32_t)nch) return -1;
+        const unsigned long long old = atomicCAS(word, w, w + 1);
+        if (old == w) {
+            *count = 1;
+            return (int)(uint32_t)w;
+        }
+        w = old;
+    }
+    return -1;
 }
 constexpr long long kHelperBudget = 20000000ll;   // ~10 ms of SM clock: helpers leave after it whatever happens
 constexpr long long kPassWaitBudget = 4000000ll;  // ~2 ms: a walker's wait for its helpers' last chunks
