@@ -511,9 +511,9 @@ __device__ uint64_t resid_chunk_sum(const char *prow, const char *qrow, int c0, 
 //          in STOCH_DRAFT the q row (qfr, qsums).
 // The walking block publishes the pass (kind, visited node, level L, row
 // statistics, frames, invT) and opens it by writing `word` = (generation << 32)
-// | 0. A warp (of the walker or a helper) takes the next chunk by a
-// compare-and-swap of `word` from (generation, j) to (generation, j + 1), so a
-// claim never takes a chunk of another pass. Each warp computes its chunk,
+// | 0. A warp (of the walker or a helper) takes the next chunk by adding 1 to
+// `word`; the value returned names the pass and the chunk, and the warp reads
+// that pass's parameters after the claim. Each warp computes its chunk,
 // stores the results and counts the chunk in `done`. The walker publishes the next pass only after `done`
 // reached the chunk count of the last, so no late write lands in a newer pass.
 // The walker claims chunks too, so a pass finishes even when no helper runs.
@@ -542,26 +542,21 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const void *p) {
     asm volatile("ld.relaxed.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
     return v;
 }
-// Claim the next chunk of pass `gen` (one thread): returns it and sets
-// *count to 1, or sets *count to 0 when every chunk of the pass is taken or
-// the pass is no longer the open one. A compare-and-swap that names the
-// generation, so a claim can never advance a newer pass's count (a helper
-// that read an older word while the walker reopened the slot fails instead).
-__device__ int claim_chunks(unsigned long long *word, uint32_t gen, int nch, int want, int *count) {
-    (void)want;
-    *count = 0;
-    unsigned long long w = ld_relaxed_u64(word);
-    for (int tries = 0; tries < 256; ++tries) {
-        if ((uint32_t)(w >> 32) != gen || (uint32_t)w >= (uint32_t)nch) return -1;
-        const unsigned long long old = atomicCAS(word, w, w + 1);
-        if (old == w) {
-            *count = 1;
-            return (int)(uint32_t)w;
-        }
-        w = old;
-    }
-    return -1;
+// Claim the next chunk of whatever pass `word` holds open (one thread): one
+// atomic add; returns the chunk, or -1 when every chunk of that pass is taken
+// (or the slot is closed). The returned chunk belongs to the pass named by the
+// word's generation at the moment of the add, which may be newer than the one
+// the caller saw: the caller computes it under that pass, reading the pass's
+// parameters after the claim. The walker rewrites the parameters only after
+// every chunk of the previous pass is done, so they cannot change under a
+// claimed chunk, and no claim is ever dropped.
+__device__ __forceinline__ int claim_chunk(unsigned long long *word, int nch) {
+    const unsigned long long w = atomicAdd(word, 1ull);
+    return (uint32_t)w < (uint32_t)nch ? (int)(uint32_t)w : -1;
 }
+// A closed slot: the count sits far above any chunk count, so late adds
+// neither claim anything nor carry into the generation.
+constexpr unsigned long long kClosedCount = 0x80000000ull;
 constexpr long long kHelperBudget = 20000000ll;   // ~10 ms of SM clock: helpers leave after it whatever happens
 constexpr long long kPassWaitBudget = 4000000ll;  // ~2 ms: a walker's wait for its helpers' last chunks
 
@@ -639,13 +634,8 @@ __device__ void help_passes(const AcceptArgs &a, int warp, int lane, bool until_
             for (unsigned m = open; m && j < 0; m &= m - 1) {
                 const int src = __ffs(m) - 1;
                 const int cb = __shfl_sync(0xffffffffu, bb, src);
-                const uint32_t cg = __shfl_sync(0xffffffffu, g, src);
                 int jj = -1;
-                if (lane == 0) {
-                    int n = 0;
-                    jj = claim_chunks(&job_of(a, cb)->word, cg, a.nch, 1, &n);
-                    if (!n) jj = -1;
-                }
+                if (lane == 0) jj = claim_chunk(&job_of(a, cb)->word, a.nch);
                 jj = __shfl_sync(0xffffffffu, jj, 0);
                 if (jj >= 0) {
                     b = cb;
@@ -970,11 +960,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         const RowStat ps = sm.ps, qs = sm.qs;
         for (;;) {  // this block takes chunks too, one warp at a time
             int j = -1;
-            if (lane == 0) {
-                int n = 0;
-                j = claim_chunks(&job->word, gen, nch, 1, &n);
-                if (!n) j = -1;
-            }
+            if (lane == 0) j = claim_chunk(&job->word, nch);
             j = __shfl_sync(0xffffffffu, j, 0);
             if (j < 0) break;
             pass_chunk<MODE, BF16>(a, b, kind, nd, L, ps, qs, sm.invT, j, lane);
@@ -990,7 +976,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
             if (!all) {
                 // never reuse this pass slot (a late chunk could land in a newer
                 // pass): close it and compute the rest of the walk in this block
-                atomicExch(&job->word, ((unsigned long long)gen << 32) | 0xFFFFFFFFull);
+                atomicExch(&job->word, ((unsigned long long)gen << 32) | kClosedCount);
                 sm.no_helpers = 1;
             }
             atomicSub(a.open_passes, 1);
