@@ -17,10 +17,10 @@ from ._lib import (A11Error, BF16, EBOUNDS, ECUDA, EINVAL, ENONFINITE, ENOSPACE,
                    EUNSUPPORTED, F32, GREEDY, OK, PAGE_TOKENS, STATS_LEN, STAT_NAMES, STOCH_DRAFT,
                    STOCH_ONEHOT, LIB_PATH)
 from . import ops
-from .ops import (AcceptResult, KVPagePool, accept, history_from_accept, kv_compact, next_roots, ngram_bucket,
-                  ngram_expand, ngram_update, read_status, tree_attention)
+from .ops import (AcceptResult, KVPagePool, accept, history_from_accept, kv_compact, lm_head, next_roots,
+                  ngram_bucket, ngram_expand, ngram_update, read_status, tree_attention)
 
-__all__ = ["A11Error", "AcceptResult", "KVPagePool", "accept", "history_from_accept", "kv_compact",
+__all__ = ["A11Error", "AcceptResult", "KVPagePool", "accept", "history_from_accept", "kv_compact", "lm_head",
            "next_roots", "ngram_bucket", "ngram_expand", "ngram_update",
            "read_status", "tree_attention", "ops", "GREEDY", "STOCH_ONEHOT", "STOCH_DRAFT", "F32",
            "BF16", "PAGE_TOKENS", "STATS_LEN", "STAT_NAMES", "LIB_PATH"]

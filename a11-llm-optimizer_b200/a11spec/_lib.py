@@ -68,10 +68,15 @@ def _load() -> C.CDLL:
     lib.a11s_kv_reserve.argtypes = [vp, vp, i32, vp, i32, vp, vp, i32, vp, vp]
     lib.a11s_kv_release.argtypes = [vp, vp, i32, vp, i32, vp, i32, vp, vp]
     lib.a11s_kv_free_sequences.argtypes = [vp, vp, i32, vp, i32, vp, vp, i32, vp, vp]
+    lib.a11s_lm_head_keys_bytes.restype = sz
+    lib.a11s_lm_head_keys_bytes.argtypes = [i32, i32]
+    lib.a11s_lm_head.argtypes = [vp, vp, i32, i32, i32, f32, vp, i64, vp, vp, sz, vp]
+    lib.a11s_accept_recorded.argtypes = [i32, vp, i64, f32, vp, vp, vp, vp, i32, i32, i32, vp, vp, vp, vp, vp,
+                                         vp, vp, vp, sz, vp]
     for name in ("a11s_read_status", "a11s_accept", "a11s_tree_attention", "a11s_kv_compact",
                  "a11s_ngram_expand", "a11s_verify_chain", "a11s_accept_static", "a11s_kv_pool_init",
                  "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update",
-                 "a11s_next_roots"):
+                 "a11s_next_roots", "a11s_lm_head", "a11s_accept_recorded"):
         getattr(lib, name).restype = C.c_int
     if lib.a11s_abi_version() != 1:
         raise ImportError("liba11spec.so ABI version mismatch")
@@ -93,4 +98,4 @@ def symbols():
             "a11s_tree_attention_workspace_bytes", "a11s_tree_attention", "a11s_kv_compact",
             "a11s_ngram_expand", "a11s_ngram_bucket", "a11s_verify_chain", "a11s_kv_pool_init",
             "a11s_kv_reserve", "a11s_kv_release", "a11s_kv_free_sequences", "a11s_ngram_update",
-            "a11s_next_roots"]
+            "a11s_next_roots", "a11s_lm_head_keys_bytes", "a11s_lm_head", "a11s_accept_recorded"]

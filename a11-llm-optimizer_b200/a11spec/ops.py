@@ -82,8 +82,12 @@ def accept(mode: int, target_logits: torch.Tensor, tokens: torch.Tensor, parents
            temperature: float = 1.0, uniforms: Optional[torch.Tensor] = None,
            stats: Optional[torch.Tensor] = None, want_node_probs: bool = False,
            ws: Optional[torch.Tensor] = None, out: Optional[AcceptResult] = None,
-           check_status: bool = False) -> AcceptResult:
-    """K3. target_logits [B, N, V] (fp32 or bf16, rows contiguous)."""
+           check_status: bool = False, keys: Optional[torch.Tensor] = None) -> AcceptResult:
+    """K3. target_logits [B, N, V] (fp32 or bf16, rows contiguous).
+
+    keys: the chunk keys of lm_head for these rows ([B * N, ceil(V / 2048)]
+    int64): the records come from them instead of a pass over the logits
+    (a11s_accept_recorded; GREEDY or STOCH_ONEHOT on bf16 logits)."""
     B, N, V = target_logits.shape
     dt = {torch.float32: _lib.F32, torch.bfloat16: _lib.BF16}.get(target_logits.dtype)
     if dt is None:
@@ -108,12 +112,23 @@ def accept(mode: int, target_logits: torch.Tensor, tokens: torch.Tensor, parents
             bonus=torch.empty(B, dtype=torch.int32, device=dev),
             node_probs=torch.empty(B, N, dtype=torch.float32, device=dev) if want_node_probs else None,
             workspace=ws if ws is not None else workspace(accept_workspace_bytes(mode, B, N, V), dev))
-    rc = lib.a11s_accept(mode, dt, target_logits.data_ptr(), _ptr(draft_logits), V,
-                         float(temperature), _ptr(uniforms), tokens.data_ptr(), parents.data_ptr(),
-                         _ptr(n_nodes), B, N, V, out.accept_len.data_ptr(),
-                         out.accepted_nodes.data_ptr(), out.accepted_tokens.data_ptr(),
-                         out.bonus.data_ptr(), _ptr(out.node_probs), _ptr(stats),
-                         out.workspace.data_ptr(), out.workspace.numel(), _stream())
+    if keys is not None:
+        _need(keys, "keys", torch.int64)
+        if draft_logits is not None:
+            raise A11Error(_lib.EUNSUPPORTED, "chunk keys cover the target rows only")
+        rc = lib.a11s_accept_recorded(mode, target_logits.data_ptr(), V, float(temperature), _ptr(uniforms),
+                                      tokens.data_ptr(), parents.data_ptr(), _ptr(n_nodes), B, N, V,
+                                      keys.data_ptr(), out.accept_len.data_ptr(), out.accepted_nodes.data_ptr(),
+                                      out.accepted_tokens.data_ptr(), out.bonus.data_ptr(),
+                                      _ptr(out.node_probs), _ptr(stats), out.workspace.data_ptr(),
+                                      out.workspace.numel(), _stream())
+    else:
+        rc = lib.a11s_accept(mode, dt, target_logits.data_ptr(), _ptr(draft_logits), V,
+                             float(temperature), _ptr(uniforms), tokens.data_ptr(), parents.data_ptr(),
+                             _ptr(n_nodes), B, N, V, out.accept_len.data_ptr(),
+                             out.accepted_nodes.data_ptr(), out.accepted_tokens.data_ptr(),
+                             out.bonus.data_ptr(), _ptr(out.node_probs), _ptr(stats),
+                             out.workspace.data_ptr(), out.workspace.numel(), _stream())
     check(rc)
     if check_status:
         raise_on_status(out.workspace)
@@ -162,6 +177,46 @@ def tree_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
     if check_status:
         raise_on_status(ws)
     return out, lse, ws
+
+
+# --------------------------------------------------------------------------- K7
+def lm_head_keys_bytes(rows: int, vocab: int) -> int:
+    return int(lib.a11s_lm_head_keys_bytes(rows, vocab))
+
+
+def lm_head(hidden: torch.Tensor, weight: torch.Tensor, out: Optional[torch.Tensor] = None,
+            keys: Optional[torch.Tensor] = None, want_keys: bool = False, scale: float = 1.0,
+            ws: Optional[torch.Tensor] = None, check_status: bool = False):
+    """K7. hidden [..., H] bf16, weight [V, H] bf16 -> logits [..., V] bf16
+    (out may be a view with a row stride >= V), and the chunk keys
+    [rows, ceil(V / 2048)] int64 when want_keys (or keys) is given."""
+    H = hidden.shape[-1]
+    V, H2 = weight.shape
+    if H2 != H:
+        raise A11Error(_lib.EINVAL, "weight must be [vocab, hidden_dim]")
+    _need(hidden, "hidden", torch.bfloat16)
+    _need(weight, "weight", torch.bfloat16)
+    rows = hidden.numel() // H
+    dev = hidden.device
+    if out is None:
+        out = torch.empty(*hidden.shape[:-1], V, dtype=torch.bfloat16, device=dev)
+    if out.dtype != torch.bfloat16 or out.device != dev or out.shape[-1] != V or out.stride(-1) != 1:
+        raise A11Error(_lib.EINVAL, "out must be bf16 [..., vocab] with unit column stride on the device")
+    row_stride = out.stride(-2) if out.dim() >= 2 else V
+    if out.numel() and any(out.stride(d) != out.stride(d + 1) * out.shape[d + 1] for d in range(out.dim() - 2)):
+        raise A11Error(_lib.EINVAL, "out rows must be evenly spaced")
+    if keys is None and want_keys:
+        keys = torch.empty(rows, (V + 2047) // 2048, dtype=torch.int64, device=dev)
+    if keys is not None:
+        _need(keys, "keys", torch.int64)
+    if ws is None:
+        ws = workspace(256, dev)
+    rc = lib.a11s_lm_head(hidden.data_ptr(), weight.data_ptr(), rows, H, V, float(scale), out.data_ptr(),
+                          int(row_stride), _ptr(keys), ws.data_ptr(), ws.numel(), _stream())
+    check(rc)
+    if check_status:
+        raise_on_status(ws)
+    return out, keys, ws
 
 
 # --------------------------------------------------------------------------- K4

@@ -393,6 +393,19 @@ __device__ void row_stats_into(const char *row, const float *root_cmax, const un
 // canonical NaN 0x7FFFFFFF; positions are >= 0). So a record that differs from
 // it is final, and a row is complete when all its records are.
 constexpr uint32_t kUnrecorded = 0xFFFFFFFFu;
+
+// A chunk key of the LM head (a11s_lm_head): bits 32-47 hold the order image
+// of the chunk's bf16 maximum (sign set -> 16 bits flipped, else sign bit set;
+// -0 stored as +0), the low 32 bits the complement of its first position.
+// A key never written (0) decodes to NaN.
+__device__ __forceinline__ float key_value(unsigned long long key) {
+    const uint32_t o = (uint32_t)(key >> 32) & 0xFFFFu;
+    const uint32_t h = (o & 0x8000u) ? (o & 0x7FFFu) : (~o & 0xFFFFu);
+    return __uint_as_float(h << 16);
+}
+__device__ __forceinline__ int32_t key_first(unsigned long long key) {
+    return (int32_t)(0xFFFFFFFFu - (uint32_t)key);
+}
 constexpr long long kRecordWaitBudget = 4000000ll;  // ~2 ms of SM clock
 __device__ __forceinline__ void st_relaxed(void *p, uint32_t v) {
     asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -826,7 +839,9 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     const int n_root_units = kRootRows * a.nch;
     int u0 = 0, u1 = 0;
     if (blockIdx.y == 0 && a.root_blocks == 0) {
-        u1 = n_root_units;  // GREEDY: the walker records its root itself (maxima only, cheap)
+        // GREEDY: the walker records its root itself (maxima only, cheap);
+        // with chunk keys every record is written before the launch
+        u1 = a.keys ? 0 : n_root_units;
     } else if (blockIdx.y >= 1 && (int)blockIdx.y <= a.root_blocks) {
         u0 = (blockIdx.y - 1) * kWarps;
         u1 = min(u0 + kWarps, n_root_units);
@@ -854,8 +869,11 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         const char *row = reinterpret_cast<const char *>(isq ? a.draft : a.target) + ((size_t)b * a.N + node) * row_bytes;
         const int c0 = j * A11S_CHUNK, clen = min(A11S_CHUNK, a.V - c0);
         int first = 0;
-        const float m = MODE == A11S_ACCEPT_GREEDY ? chunk_max_first<BF16>(row, c0, clen, lane, first)
-                                                   : chunk_max<BF16>(row, c0, clen, lane);
+        // with chunk keys only the root units of the sampling modes run here:
+        // the maximum comes from the key, the weight sums from the row
+        const float m = a.keys ? key_value(__ldg(a.keys + ((size_t)b * a.N + node) * a.nch + j))
+                        : MODE == A11S_ACCEPT_GREEDY ? chunk_max_first<BF16>(row, c0, clen, lane, first)
+                                                     : chunk_max<BF16>(row, c0, clen, lane);
         bad |= !(m < INFINITY);  // the NaN-propagating max is NaN or +Inf
         if (MODE != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = 1;
         const size_t rrow = (size_t)b * a.rows_per_seq + r;
@@ -1376,6 +1394,45 @@ cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, void *z
     const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 4 * 148);
     accept_init_kernel<<<blocks ? blocks : 1, 256, 0, s>>>(st, reinterpret_cast<uint4 *>(recs), n16,
                                                            reinterpret_cast<uint4 *>(zero), z16);
+    return cudaGetLastError();
+}
+
+__global__ void accept_keys_init_kernel(const AcceptArgs a, int mode, uint4 *zero, size_t z16) {
+    const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
+    if (i0 == 0) {
+        *a.status = StatusWord{};
+        reinterpret_cast<uint4 *>(a.status)[1] = make_uint4(0, 0, 0, 0);  // the walk counters at bytes 16 and 20
+    }
+    for (size_t i = i0; i < z16; i += step) zero[i] = make_uint4(0, 0, 0, 0);
+    // records [B][N][nch] (rows_per_seq == N in GREEDY and STOCH_ONEHOT), the keys in the same order
+    const size_t n = (size_t)a.B * a.N * a.nch;
+    for (size_t i = i0; i < n; i += step) {
+        const size_t r = i / (size_t)a.nch;
+        const int node = (int)(r % (size_t)a.N), b = (int)(r / (size_t)a.N);
+        int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
+        if (n_live < 1 || n_live > a.N) n_live = 0;  // the acceptance kernel reports the bad count
+        uint32_t rec = kUnrecorded;
+        if (node < n_live) {
+            const unsigned long long key = a.keys[i];
+            const float m = key_value(key);
+            bool bad = !(m < INFINITY);  // NaN or +Inf, as the pass over the logits finds it
+            if (mode != A11S_ACCEPT_GREEDY && m > -INFINITY && !(fabsf(__fmul_rn(m, a.k)) < 16777216.0f)) bad = true;
+            if (bad) report(a.status, A11S_ENONFINITE, b);
+            // the sampling modes' root records are published by the root blocks with their weight sums
+            if (mode == A11S_ACCEPT_GREEDY || node != 0) rec = __float_as_uint(m);
+            if (mode == A11S_ACCEPT_GREEDY) a.arg[i] = m == m ? key_first(key) : INT_MAX;
+        } else if (mode == A11S_ACCEPT_GREEDY) {
+            a.arg[i] = -1;
+        }
+        reinterpret_cast<uint32_t *>(a.recs)[i] = rec;
+    }
+}
+
+cudaError_t launch_accept_keys_init(int mode, const AcceptArgs &a, void *zero, size_t zero_bytes, cudaStream_t s) {
+    const size_t n = std::max((size_t)a.B * a.N * a.nch, zero ? zero_bytes / 16 : 0);
+    const unsigned blocks = (unsigned)std::min<size_t>((n + 255) / 256, 4 * 148);
+    accept_keys_init_kernel<<<blocks ? blocks : 1, 256, 0, s>>>(a, mode, reinterpret_cast<uint4 *>(zero),
+                                                                zero ? zero_bytes / 16 : 0);
     return cudaGetLastError();
 }
 

@@ -104,13 +104,15 @@ size_t a11s_accept_workspace_bytes(int32_t mode, int32_t batch, int32_t max_node
     return accept_layout(mode, batch, max_nodes, vocab).total;
 }
 
-int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const void *draft_logits,
+namespace {
+// a11s_accept, or a11s_accept_recorded when `keys` is given.
+int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const void *draft_logits,
                 int64_t row_stride, float temperature, const float *uniforms,
                 const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes,
                 int32_t batch, int32_t max_nodes, int32_t vocab, int32_t *accept_len,
                 int32_t *accepted_nodes, int32_t *accepted_tokens, int32_t *bonus,
                 float *node_probs, int64_t *stats, void *workspace, size_t workspace_bytes,
-                void *stream) {
+                void *stream, const uint64_t *keys) {
     if (mode < A11S_ACCEPT_GREEDY || mode > A11S_ACCEPT_STOCH_DRAFT)
         return fail(A11S_EINVAL, "a11s_accept: unknown mode %d", mode);
     if (dtype != A11S_F32 && dtype != A11S_BF16)
@@ -188,6 +190,7 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     // per warp) per block.
     const int root_units = a.nch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
     a.root_blocks = mode == A11S_ACCEPT_GREEDY ? 0 : (root_units + 15) / 16;
+    a.keys = reinterpret_cast<const unsigned long long *>(keys);
     const long long rest = (long long)a.units_per_seq - root_units;
     const long long target_blocks = (long long)sm_count() * 2 * 4;
     long long slice = ((long long)batch * rest + target_blocks - 1) / target_blocks;
@@ -195,7 +198,8 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     if (slice < 16) slice = 16;
     if (slice > rest && rest > 0) slice = rest;
     a.slice = (int32_t)slice;
-    int grid_y = 1 + a.root_blocks + (int)((rest + slice - 1) / slice);
+    // with chunk keys there is nothing to stream: the walkers and the root blocks
+    int grid_y = 1 + a.root_blocks + (keys ? 0 : (int)((rest + slice - 1) / slice));
     a.bulk_rows = grid_y;
     if (mode != A11S_ACCEPT_GREEDY) {
         // Helper rows: blocks scheduled after every walking and streaming block
@@ -205,12 +209,41 @@ int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const vo
     }
 
     cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-    cudaError_t e = a11s::launch_accept_init(a.status, ws + L.recs, L.root_sums - L.recs, a.jobs,
-                                             a.jobs ? L.total - L.jobs : 0, s);
+    cudaError_t e = keys ? a11s::launch_accept_keys_init(mode, a, a.jobs, a.jobs ? L.total - L.jobs : 0, s)
+                         : a11s::launch_accept_init(a.status, ws + L.recs, L.root_sums - L.recs, a.jobs,
+                                                    a.jobs ? L.total - L.jobs : 0, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: clearing workspace");
     e = a11s::launch_accept(mode, dtype == A11S_BF16, a, grid_y, s);
     if (e != cudaSuccess) return cuda_fail(e, "a11s_accept: launch");
     return A11S_OK;
+}
+}  // namespace
+
+int a11s_accept(int32_t mode, int32_t dtype, const void *target_logits, const void *draft_logits,
+                int64_t row_stride, float temperature, const float *uniforms,
+                const int32_t *tokens, const int32_t *parents, const int32_t *n_nodes,
+                int32_t batch, int32_t max_nodes, int32_t vocab, int32_t *accept_len,
+                int32_t *accepted_nodes, int32_t *accepted_tokens, int32_t *bonus,
+                float *node_probs, int64_t *stats, void *workspace, size_t workspace_bytes,
+                void *stream) {
+    return accept_call(mode, dtype, target_logits, draft_logits, row_stride, temperature, uniforms, tokens,
+                       parents, n_nodes, batch, max_nodes, vocab, accept_len, accepted_nodes, accepted_tokens,
+                       bonus, node_probs, stats, workspace, workspace_bytes, stream, nullptr);
+}
+
+int a11s_accept_recorded(int32_t mode, const void *target_logits, int64_t row_stride, float temperature,
+                         const float *uniforms, const int32_t *tokens, const int32_t *parents,
+                         const int32_t *n_nodes, int32_t batch, int32_t max_nodes, int32_t vocab,
+                         const uint64_t *chunk_keys, int32_t *accept_len, int32_t *accepted_nodes,
+                         int32_t *accepted_tokens, int32_t *bonus, float *node_probs, int64_t *stats,
+                         void *workspace, size_t workspace_bytes, void *stream) {
+    if (mode != A11S_ACCEPT_GREEDY && mode != A11S_ACCEPT_STOCH_ONEHOT)
+        return fail(A11S_EUNSUPPORTED, "a11s_accept_recorded: mode %d (GREEDY or STOCH_ONEHOT only)", mode);
+    if (batch > 0 && (!chunk_keys || !aligned16(chunk_keys)))
+        return fail(A11S_EINVAL, "a11s_accept_recorded: chunk_keys must be a 16-byte aligned device pointer");
+    return accept_call(mode, A11S_BF16, target_logits, nullptr, row_stride, temperature, uniforms, tokens,
+                       parents, n_nodes, batch, max_nodes, vocab, accept_len, accepted_nodes, accepted_tokens,
+                       bonus, node_probs, stats, workspace, workspace_bytes, stream, chunk_keys);
 }
 
 int a11s_verify_chain(const float *draft_probs, const float *target_probs, const float *uniforms,
@@ -407,6 +440,45 @@ int a11s_kv_free_sequences(int32_t *free_stack, int32_t *free_top, int32_t num_p
                         batch, status};
     cudaError_t e = a11s::launch_kv_push(a, true, reinterpret_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return cuda_fail(e, "a11s_kv_free_sequences: launch");
+    return A11S_OK;
+}
+
+// ------------------------------------------------------------------- K7
+size_t a11s_lm_head_keys_bytes(int32_t rows, int32_t vocab) {
+    if (rows < 0 || vocab < 1) return 0;
+    return (size_t)rows * (size_t)((vocab + A11S_CHUNK - 1) / A11S_CHUNK) * sizeof(uint64_t);
+}
+
+int a11s_lm_head(const void *hidden, const void *weight, int32_t rows, int32_t hidden_dim, int32_t vocab,
+                 float scale, void *logits, int64_t row_stride, uint64_t *chunk_keys,
+                 void *workspace, size_t workspace_bytes, void *stream) {
+    if (rows < 0 || hidden_dim < 8 || vocab < 8) return fail(A11S_EINVAL, "a11s_lm_head: bad sizes");
+    if (hidden_dim % 8 || vocab % 8 || row_stride % 8)
+        return fail(A11S_EINVAL, "a11s_lm_head: hidden_dim, vocab and row_stride must be multiples of 8");
+    if (row_stride < vocab) return fail(A11S_EINVAL, "a11s_lm_head: row_stride %lld < vocab %d", (long long)row_stride, vocab);
+    if (!std::isfinite(scale)) return fail(A11S_EINVAL, "a11s_lm_head: scale is not finite");
+    if (rows == 0) return empty_batch_status(workspace, workspace_bytes, stream, "a11s_lm_head: clearing status");
+    if (!hidden || !weight || !logits || !workspace) return fail(A11S_EINVAL, "a11s_lm_head: null required pointer");
+    if (!aligned16(hidden) || !aligned16(weight) || !aligned16(logits) || !aligned16(workspace) ||
+        (chunk_keys && !aligned16(chunk_keys)))
+        return fail(A11S_EINVAL, "a11s_lm_head: tensors must be 16-byte aligned");
+    if (workspace_bytes < 256) return fail(A11S_ENOSPACE, "a11s_lm_head: workspace %zu < 256 bytes", workspace_bytes);
+    cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+    cudaError_t e = cudaMemsetAsync(workspace, 0, sizeof(a11s::StatusWord), s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_lm_head: clearing status");
+    a11s::LmHeadArgs a{};
+    a.hidden = hidden;
+    a.weight = weight;
+    a.rows = rows;
+    a.V = vocab;
+    a.K = hidden_dim;
+    a.scale = scale;
+    a.logits = logits;
+    a.ldl = row_stride;
+    a.keys = reinterpret_cast<unsigned long long *>(chunk_keys);
+    a.status = reinterpret_cast<a11s::StatusWord *>(workspace);
+    e = a11s::launch_lm_head(a, s);
+    if (e != cudaSuccess) return cuda_fail(e, "a11s_lm_head: launch");
     return A11S_OK;
 }
 

@@ -40,14 +40,33 @@ struct AcceptArgs {
     int32_t *open_passes;  // passes published and not yet complete
     int32_t bulk_rows;    // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
     int32_t root_blocks;  // grid rows 1 .. root_blocks take the root units, one per warp (0: the walker does)
+    const unsigned long long *keys;  // chunk keys of the LM head ([B * N][nch]): records come from them, no bulk pass
 };
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s);
+
+struct LmHeadArgs {
+    const void *hidden;  // bf16 [rows][K]
+    const void *weight;  // bf16 [V][K]
+    int32_t rows, V;
+    int64_t K;
+    float scale;
+    void *logits;        // bf16 [rows][ldl]
+    int64_t ldl;
+    unsigned long long *keys;  // [rows][ceil(V / 2048)] or null
+    StatusWord *status;
+};
+cudaError_t launch_lm_head(const LmHeadArgs &a, cudaStream_t s);
 // Clears the status word and the 16 bytes after it, marks every record unwritten
 // (bytes: a multiple of 16) and zeroes `zero_bytes` at `zero` (a multiple of 16;
 // nullable).
 cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, void *zero, size_t zero_bytes,
                                cudaStream_t s);
+// Recorded mode: clears the status word and its counters, zeroes the jobs
+// area, and writes every live row's records from the chunk keys (the root
+// rows' stay unwritten in the sampling modes: the root blocks publish them
+// with their weight sums); reports ENONFINITE for a NaN / +Inf maximum.
+cudaError_t launch_accept_keys_init(int mode, const AcceptArgs &a, void *zero, size_t zero_bytes, cudaStream_t s);
 // Bytes of one sequence's shared-pass area (sampling modes).
 size_t accept_job_bytes(int nch);
 

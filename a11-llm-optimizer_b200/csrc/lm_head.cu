@@ -1,0 +1,382 @@
+// lm_head.cu - K7: the tree-node LM head on the tensor cores (TMA + tcgen05,
+// TMEM accumulators, sm_100a), with the acceptance's chunk records folded
+// into its epilogue.
+//
+// logits[r][v] = bf16_rn(scale * sum_k hidden[r][k] * weight[v][k]), fp32 accumulation:
+// the `torch.matmul(h_norm, output_w.t())` of A11Pipeline.forward_token
+// (engine/pipeline.py:468-472) for every tree node at once, the job of
+// tree_forward_pass_kernel (src/cuda/tree_verification.cu:34-68).
+// keys[r][j] (nullable): the maximum of row r's bf16 logits in 2048-token chunk
+// j and its first position, one 64-bit key per (row, chunk): the order image
+// of the value (lm_order2) above the complement of the position, combined over
+// the chunk's 8 tiles with atomicMax. The acceptance kernel turns them into
+// its chunk records instead of streaming the logits once more.
+// Semantics: include/a11spec.h (a11s_lm_head).
+//
+// Persistent kernel, one CTA per SM, tiles of 128 rows x 256 vocabulary
+// entries taken m-fastest, so the CTAs at work at one time share a weight tile
+// (read from HBM once) and the hidden states stay in L2. 192 threads:
+//   warp 0     TMA producer: K slices of 64 of the hidden tile (128 x 64) and
+//              the weight tile (256 x 64) into a 4-stage ring, 128-byte swizzle
+//   warp 1     TMEM allocator and MMA issuer: per K slice 4 x tcgen05.mma
+//              M128 N256 K16, both operands K-major in shared memory, into one
+//              of two accumulators of 256 TMEM columns
+//   warps 2-5  epilogue (thread = tile row = TMEM lane): 128 columns per TMEM
+//              load, bf16 rounding (nearest even), the chunk key on packed
+//              pairs, the bf16 tile staged in swizzled shared memory and
+//              written by TMA stores (clipped at the vocabulary and the last
+//              row). The accumulator is released after its last load, so the
+//              epilogue of tile i runs under the MMAs of tile i + 1.
+// Every mbarrier wait is bounded; a timeout sets ETIMEOUT, and the CTA drains
+// its copies and MMAs and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "tc_common.cuh"
+
+namespace a11s {
+
+namespace {
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kStages = 4;
+constexpr uint32_t kABytes = kBM * kBK * 2;               // 16 KB
+constexpr uint32_t kBBytes = kBN * kBK * 2;               // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;       // 48 KB
+constexpr uint32_t kBoxBytes = 32 * 128;                  // one stored box: 32 rows x 64 columns
+constexpr uint32_t kStageWarpBytes = 2 * kBoxBytes;       // an epilogue warp's staging area
+constexpr uint32_t kOffStage = kStages * kStageBytes;     // 196608
+constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarpBytes;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;     // + barriers + alignment slack
+static_assert(kSmemBytes <= 232448, "shared memory budget");
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 2 * kBN;
+constexpr uint32_t kIdesc = tc::idesc_bf16_f32(kBM, kBN, false);
+constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
+static_assert(A11S_CHUNK % kBN == 0, "a tile lies inside one chunk");
+
+struct Bars {
+    uint64_t full[kStages], empty[kStages];
+    uint64_t acc_full[2], acc_empty[2];
+    uint64_t drain;
+    uint32_t tmem_base;
+    int32_t abort;
+};
+static_assert(sizeof(Bars) <= 256, "barrier block");
+
+struct LmParams {
+    __nv_bfloat16 *logits;
+    int64_t ldl;
+    unsigned long long *keys;
+    float scale;
+    int32_t rows, V, nch, m_tiles, n_tiles, k_blocks;
+    StatusWord *status;
+};
+
+__device__ __forceinline__ bool aborted(Bars *bs) { return *reinterpret_cast<volatile int32_t *>(&bs->abort) != 0; }
+
+__device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, Bars *bs, StatusWord *st) {
+    if (tc::mbar_wait(bar, parity, kWaitBudget)) return true;
+    *reinterpret_cast<volatile int32_t *>(&bs->abort) = 1;
+    report(st, A11S_ETIMEOUT, (int32_t)blockIdx.x);
+    return false;
+}
+}  // namespace
+
+// Order-preserving images of a bf16 pair for an unsigned maximum, per half:
+// sign set -> all 16 bits flipped, else the sign bit set. -0 (0x7FFF) then
+// sits just below +0 (0x8000); the key treats them as equal (below).
+__device__ __forceinline__ uint32_t lm_order2(uint32_t w) {
+    const uint32_t s = (w >> 15) & 0x00010001u;
+    return w ^ (s * 0x7FFFu + 0x80008000u);
+}
+__device__ __forceinline__ uint32_t lm_max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+__device__ __forceinline__ uint32_t lm_max_nan_bf16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.NaN.bf16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Chunk key of 128 columns (col0 .. col0 + 127 of the tile; w = their bf16
+// pairs) folded into (best, best_col): the largest ordered value, -0 taken as
+// +0 and any NaN as the largest (0xFFFF), and the first column holding it.
+// Columns at or past `valid` take no part. A later half replaces the best
+// only when strictly larger, so the first position wins ties.
+__device__ __forceinline__ void lm_half_key(const uint32_t (&w)[64], int col0, int valid, uint32_t &best,
+                                            int &best_col) {
+    uint32_t o[64];
+    uint32_t mx = 0, nan = 0;
+#pragma unroll
+    for (int e = 0; e < 64; ++e) {
+        o[e] = lm_order2(w[e]);
+        nan = lm_max_nan_bf16x2(nan, w[e]);
+    }
+    if ((nan & 0x7FFFu) > 0x7F80u || (nan >> 16 & 0x7FFFu) > 0x7F80u) {  // a NaN: it is the maximum
+#pragma unroll
+        for (int e = 0; e < 64; ++e) {
+            if ((w[e] & 0x7FFFu) > 0x7F80u) o[e] |= 0xFFFFu;
+            if ((w[e] >> 16 & 0x7FFFu) > 0x7F80u) o[e] |= 0xFFFF0000u;
+        }
+    }
+    if (col0 + 128 > valid) {  // the vocabulary ends in this half (valid is a multiple of 8)
+#pragma unroll
+        for (int e = 0; e < 64; ++e)
+            if (col0 + 2 * e >= valid) o[e] = 0u;
+    }
+#pragma unroll
+    for (int e = 0; e < 64; ++e) mx = lm_max_u16x2(mx, o[e]);
+    uint32_t M = max(mx & 0xFFFFu, mx >> 16);
+    if (M == 0x7FFFu) M = 0x8000u;  // a zero maximum: -0 counts as +0
+    if (M > best) {
+        const uint32_t Mz = M == 0x8000u ? 0x7FFFu : M;  // and matches either sign
+        int pos = 0;
+#pragma unroll
+        for (int e = 63; e >= 0; --e) {
+            const uint32_t lo = o[e] & 0xFFFFu, hi = o[e] >> 16;
+            if (hi == M || hi == Mz) pos = 2 * e + 1;
+            if (lo == M || lo == Mz) pos = 2 * e;
+        }
+        best = M;
+        best_col = col0 + pos;
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    lm_head_tc(const __grid_constant__ CUtensorMap ta, const __grid_constant__ CUtensorMap tb,
+               const __grid_constant__ CUtensorMap tc_out, const LmParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    Bars *bs = reinterpret_cast<Bars *>(sm + kOffBar);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int total = p.m_tiles * p.n_tiles;
+    const int my_tiles = (int)blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    if (my_tiles == 0) return;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            tc::mbar_init(&bs->full[s], 1);
+            tc::mbar_init(&bs->empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&bs->acc_full[b], 1);
+            tc::mbar_init(&bs->acc_empty[b], 4);  // one arrival per epilogue warp
+        }
+        tc::mbar_init(&bs->drain, 1);
+        bs->abort = 0;
+        tc::fence_barrier_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(&bs->tmem_base, kTmemCols);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = bs->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            tc::prefetch_tmap(&ta);
+            tc::prefetch_tmap(&tb);
+            tc::prefetch_tmap(&tc_out);
+            int it = 0;  // K slices issued
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                const int t = (int)blockIdx.x + i * (int)gridDim.x;
+                const int m0 = (t % p.m_tiles) * kBM, n0 = (t / p.m_tiles) * kBN;
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    const int s = it % kStages, use = it / kStages;
+                    // the slot was last read by the MMAs of slice it - kStages
+                    if (use > 0 && !(ok = wait_or_abort(&bs->empty[s], (use - 1) & 1, bs, p.status))) break;
+                    if (aborted(bs)) {
+                        ok = false;
+                        break;
+                    }
+                    uint8_t *sa = sm + s * kStageBytes;
+                    tc::mbar_arrive_expect_tx(&bs->full[s], kStageBytes);
+                    tc::tma_load_2d(sa, &ta, &bs->full[s], kb * kBK, m0);
+                    tc::tma_load_2d(sa + kABytes, &tb, &bs->full[s], kb * kBK, n0);
+                    ++it;
+                }
+            }
+            if (!ok) {  // copies that may still be landing in this CTA's shared memory
+                for (int j = max(0, it - kStages); j < it; ++j)
+                    tc::mbar_wait(&bs->full[j % kStages], (j / kStages) & 1, kWaitBudget);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int i = 0; i < my_tiles && ok; ++i) {
+                const int buf = i & 1, use = i >> 1;
+                // the epilogue of tile i - 2 has read this accumulator
+                if (use > 0 && !(ok = wait_or_abort(&bs->acc_empty[buf], (use - 1) & 1, bs, p.status))) break;
+                tc::tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(buf * kBN);
+                for (int kb = 0; kb < p.k_blocks; ++kb) {
+                    const int s = it % kStages;
+                    if (!(ok = wait_or_abort(&bs->full[s], (it / kStages) & 1, bs, p.status))) break;
+                    tc::tc_fence_after();
+                    const uint32_t a_addr = tc::smem_u32(sm + s * kStageBytes), b_addr = a_addr + kABytes;
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        tc::mma_bf16_ss(d, tc::sdesc_sw128(a_addr + kk * 32, 16, 1024),
+                                        tc::sdesc_sw128(b_addr + kk * 32, 16, 1024), kIdesc,
+                                        (kb | kk) != 0 ? 1u : 0u);
+                    tc::mma_commit(&bs->empty[s]);
+                    ++it;
+                }
+                if (ok) tc::mma_commit(&bs->acc_full[buf]);
+            }
+            // every issued MMA completes before the CTA may release TMEM
+            tc::mma_commit(&bs->drain);
+            tc::mbar_wait(&bs->drain, 0, kWaitBudget);
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: warp w reads TMEM lanes 32 (w % 4) .. + 31 ----------------
+        const int q = warp & 3;
+        const uint32_t lane_base = (uint32_t)(q * 32) << 16;
+        // this warp's staging area: two 64-column boxes of its 32 rows (128 B
+        // per row, 128-byte swizzle: 16-byte chunk c of row r at c ^ (r & 7))
+        uint8_t *stage = sm + kOffStage + q * kStageWarpBytes;
+        const uint32_t srow = tc::smem_u32(stage) + (uint32_t)lane * 128u;
+        bool ok = true;
+        for (int i = 0; i < my_tiles && ok; ++i) {
+            const int t = (int)blockIdx.x + i * (int)gridDim.x;
+            const int m0 = (t % p.m_tiles) * kBM, n0 = (t / p.m_tiles) * kBN;
+            const int buf = i & 1;
+            if (!(ok = __all_sync(0xffffffffu, wait_or_abort(&bs->acc_full[buf], (i >> 1) & 1, bs, p.status)))) break;
+            tc::tc_fence_after();
+            const int row = m0 + q * 32 + lane;
+            const int valid = min(kBN, p.V - n0);  // columns inside the vocabulary (a multiple of 8)
+            uint32_t best = 0;                     // below every key: the order of -inf is 0x7F
+            int best_col = 0;
+#pragma unroll 1
+            for (int half = 0; half < 2; ++half) {
+                uint32_t w[64];
+                {
+                    float v[128];
+                    tc::tmem_ld128(tmem + lane_base + (uint32_t)(buf * kBN + half * 128), v);
+                    if (half == 1) {  // the accumulator is in registers: the next tile may use it
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&bs->acc_empty[buf]);
+                    }
+#pragma unroll
+                    for (int e = 0; e < 64; ++e)
+                        w[e] = tc::cvt_bf16x2(__fmul_rn(v[2 * e], p.scale), __fmul_rn(v[2 * e + 1], p.scale));
+                }
+                if (p.keys && half * 128 < valid) lm_half_key(w, half * 128, valid, best, best_col);
+                // the previous stores from the staging area have read it
+                if (lane == 0) tc::bulk_wait_read_all();
+                __syncwarp();
+#pragma unroll
+                for (int b = 0; b < 2; ++b)
+#pragma unroll
+                    for (int c = 0; c < 8; ++c) {
+                        const uint32_t wv[4] = {w[32 * b + 4 * c], w[32 * b + 4 * c + 1], w[32 * b + 4 * c + 2],
+                                                w[32 * b + 4 * c + 3]};
+                        tc::st_shared_v4(srow + (uint32_t)b * kBoxBytes + (((uint32_t)c ^ (uint32_t)(lane & 7)) << 4), wv);
+                    }
+                tc::fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {  // clipped at the vocabulary and the last row
+                    tc::tma_store_2d(&tc_out, stage, n0 + half * 128, m0 + q * 32);
+                    tc::tma_store_2d(&tc_out, stage + kBoxBytes, n0 + half * 128 + 64, m0 + q * 32);
+                    tc::bulk_commit_group();
+                }
+            }
+            if (p.keys && row < p.rows && valid > 0) {
+                const int pos = (n0 % A11S_CHUNK) + best_col;
+                const unsigned long long key = ((unsigned long long)best << 32) | (0xFFFFFFFFu - (uint32_t)pos);
+                atomicMax(p.keys + (size_t)row * p.nch + n0 / A11S_CHUNK, key);
+            }
+        }
+        if (lane == 0) tc::bulk_wait_all();
+        __syncwarp();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------- host side
+namespace {
+PFN_cuTensorMapEncodeTiled_v12000 lm_encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *ptr = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    });
+    return fn;
+}
+
+// 2-D bf16 [outer][inner] row-major (row pitch `pitch` elements, default
+// inner), box 64 x box_rows, 128-byte swizzle.
+bool encode_rows(CUtensorMap *map, const void *base, int64_t inner, int64_t outer, uint32_t box_rows,
+                 int64_t pitch = 0) {
+    auto fn = lm_encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+    const cuuint64_t str[1] = {(cuuint64_t)(pitch > 0 ? pitch : inner) * 2};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, str, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+}  // namespace
+
+cudaError_t launch_lm_head(const LmHeadArgs &a, cudaStream_t s) {
+    CUtensorMap ta, tb;
+    if (!encode_rows(&ta, a.hidden, a.K, a.rows, kBM)) return cudaErrorInvalidValue;
+    if (!encode_rows(&tb, a.weight, a.K, a.V, kBN)) return cudaErrorInvalidValue;
+    CUtensorMap to;  // logits [rows][V] with row pitch ldl: 64 x 32 boxes, 128-byte swizzle
+    if (!encode_rows(&to, a.logits, a.V, a.rows, 32, a.ldl)) return cudaErrorInvalidValue;
+    cudaError_t e = cudaFuncSetAttribute(lm_head_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
+    if (e != cudaSuccess) return e;
+    LmParams p{};
+    p.logits = reinterpret_cast<__nv_bfloat16 *>(a.logits);
+    p.ldl = a.ldl;
+    p.keys = a.keys;
+    p.scale = a.scale;
+    p.rows = a.rows;
+    p.V = a.V;
+    p.nch = (a.V + A11S_CHUNK - 1) / A11S_CHUNK;
+    p.m_tiles = (a.rows + kBM - 1) / kBM;
+    p.n_tiles = (a.V + kBN - 1) / kBN;
+    p.k_blocks = (int32_t)((a.K + kBK - 1) / kBK);
+    p.status = a.status;
+    if (a.keys) {
+        e = cudaMemsetAsync(a.keys, 0, (size_t)a.rows * p.nch * sizeof(unsigned long long), s);
+        if (e != cudaSuccess) return e;
+    }
+    int sms = 148, dev = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long tiles = (long long)p.m_tiles * p.n_tiles;
+    const int grid = (int)std::min<long long>(tiles, sms);
+    lm_head_tc<<<grid, kThreads, kSmemBytes, s>>>(ta, tb, to, p);
+    return cudaGetLastError();
+}
+
+}  // namespace a11s

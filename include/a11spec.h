@@ -13,6 +13,7 @@
  *                         the page allocator of the paged KV cache    (K5)
  *   a11s_ngram_update     the n-gram table learns committed tokens    (K6)
  *   a11s_next_roots       next roots and committed-token rows of a step (K6 input)
+ *   a11s_lm_head          tree-node LM head, chunk records in its epilogue (K7)
  *
  * Conventions shared by every entry point
  *   - All tensor arguments are caller-owned DEVICE pointers, row-major and
@@ -140,6 +141,24 @@ int a11s_accept(int32_t mode, int32_t dtype,
                 int32_t *bonus, float *node_probs, int64_t *stats,
                 void *workspace, size_t workspace_bytes, void *stream);
 
+/* Acceptance with the chunk records taken from a11s_lm_head's chunk_keys
+ * instead of a pass over the logits: the same decisions, bonus tokens,
+ * node_probs and stats as a11s_accept on the same bf16 logits (the keys hold
+ * exactly the chunk maxima and first positions that its pass would record).
+ * Modes GREEDY and STOCH_ONEHOT (STOCH_DRAFT has draft rows the keys do not
+ * cover: A11S_EUNSUPPORTED). target_logits bf16 [batch][max_nodes] rows
+ * `row_stride` apart; chunk_keys uint64 [batch * max_nodes][ceil(vocab/2048)]
+ * of those rows. The walk still reads the logits of the rows it visits; the
+ * other rows are never read. The workspace is sized as for a11s_accept.
+ * A live row whose key holds a NaN or +Inf maximum (or was never written)
+ * reports A11S_ENONFINITE, as a11s_accept does for such a row. */
+int a11s_accept_recorded(int32_t mode, const void *target_logits, int64_t row_stride, float temperature,
+                         const float *uniforms, const int32_t *tokens, const int32_t *parents,
+                         const int32_t *n_nodes, int32_t batch, int32_t max_nodes, int32_t vocab,
+                         const uint64_t *chunk_keys, int32_t *accept_len, int32_t *accepted_nodes,
+                         int32_t *accepted_tokens, int32_t *bonus, float *node_probs, int64_t *stats,
+                         void *workspace, size_t workspace_bytes, void *stream);
+
 /* Chain acceptance on per-token probabilities: the rule of
  * SpeculativeTreeVerifier::verify_draft_tokens (src/engine/speculative_verifier.cpp:84-135)
  * for `batch` independent chains of `n` drafts. draft, target, uniforms are
@@ -183,6 +202,33 @@ int a11s_accept_static(int32_t mode, int32_t dtype,
                        int32_t *accept_len, int32_t *accepted_nodes, int32_t *accepted_tokens,
                        int32_t *bonus, float *node_probs, int64_t *stats, int32_t *status,
                        void *stream);
+
+/* ------------------------------------------------------------------------ K7
+ * Tree-node LM head on the tensor cores. Replaces the logits product of
+ * A11Pipeline.forward_token (engine/pipeline.py:468-472, `torch.matmul(h_norm,
+ * output_w.t())`) for every tree node at once, and tree_forward_pass_kernel
+ * (src/cuda/tree_verification.cu:34-68, which also divides by sqrt(hidden_dim):
+ * pass scale = 1/sqrt(hidden_dim) for that form).
+ *
+ * logits[r][v] = bf16 round-to-nearest-even of scale * sum_k hidden[r][k] *
+ *   weight[v][k], the sum in fp32 on the tensor cores (order unspecified).
+ * hidden bf16 [rows][hidden_dim]; weight bf16 [vocab][hidden_dim] (output_w as
+ * stored); logits bf16, rows `row_stride` elements apart (>= vocab).
+ * hidden_dim, vocab and row_stride multiples of 8; 16-byte aligned pointers.
+ * chunk_keys (nullable) uint64 [rows][ceil(vocab / 2048)], sized by
+ * a11s_lm_head_keys_bytes(): for each row and 2048-token chunk the maximum of
+ * the row's bf16 logits in the chunk and the first position holding it,
+ * packed for a11s_accept_recorded, which then takes its chunk records from
+ * them and never streams the logits for them. -0 counts as +0 and a NaN as
+ * the largest value.
+ * workspace >= 256 bytes (status word: A11S_ETIMEOUT if a pipeline wait of the
+ * kernel ran out).
+ */
+size_t a11s_lm_head_keys_bytes(int32_t rows, int32_t vocab);
+
+int a11s_lm_head(const void *hidden, const void *weight, int32_t rows, int32_t hidden_dim, int32_t vocab,
+                 float scale, void *logits, int64_t row_stride, uint64_t *chunk_keys,
+                 void *workspace, size_t workspace_bytes, void *stream);
 
 /* ------------------------------------------------------------------------ K2
  * Tree-masked verification attention over the paged KV pool. Replaces the
