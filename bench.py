@@ -4,15 +4,18 @@ Workload (per GPU, weak scaling): the end-to-end draft -> verify -> accept
 step of 32 sequences: hashed trigram drafting (2^20 x 8 table, Zipf(1.2)
 counts) into trees of <= 64 nodes (4 at depth 1, 2 below, depth <= 5), tree
 attention over 16-token KV pages with context 32768 (GQA 32/4, d=128, bf16),
-the LM head [nodes, 2048] x [2048, 151936] (bf16, torch/cuBLAS input stage),
-sampling acceptance at T=0.7 with seeded uniforms, and KV compaction. Inputs are
-seeded synthetic tensors (no dataset exists for this path).
+the LM head [nodes, 2048] x [151936, 2048]^T (bf16, this library's tcgen05
+kernel, which also writes the acceptance's chunk keys), sampling acceptance at
+T=0.7 with seeded uniforms (records from those keys), and KV compaction.
+Inputs are seeded synthetic tensors (no dataset exists for this path).
 
 metric: accepted tokens/s (emitted tokens = accepted drafts + bonus, summed over
 all ranks, over the max-over-ranks device time). On one GPU the line also
 carries `configs`: device time per launch and roofline fraction of the kernels
 of the four single-GPU configurations (greedy chain, greedy tree, sampling
-against draft logits, tree attention + greedy acceptance + compaction).
+against draft logits, tree attention + greedy acceptance + compaction) and of
+the C5 LM head and acceptance (with the streaming acceptance over the logits
+and cuBLAS's product for comparison).
 
 Usage:  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 Multi-GPU: launched by torch.distributed.run, one rank per GPU. The only
@@ -189,11 +192,12 @@ def device_time_us(fn, iters: int, pre=None) -> float:
 
 
 # ----------------------------------------------------------------------------- C1-C4 kernels
-def measure_configs(dev, pk) -> dict:
+def measure_configs(dev, pk, c5=None) -> dict:
     """Device time per launch of the kernels of the single-GPU configurations,
     with algorithmic bytes or FLOPs and the fraction of the measured peak.
     Between timed launches the inputs rotate over copies larger than L2 in
-    total (C1, C2), or a single copy already exceeds L2 (C3, C4)."""
+    total (C1, C2), or a single copy already exceeds L2 (C3, C4, C5).
+    c5: the C5 step's state (hidden, w_out, logits, keys, tree, uniforms)."""
     import a11spec
     from a11spec import workloads as W
 
@@ -204,6 +208,45 @@ def measure_configs(dev, pk) -> dict:
         gbs = nbytes / (us * 1e-6) / 1e9
         return {"us_per_launch": us, "bytes_per_launch": nbytes, "achieved_gbs": gbs,
                 "frac_hbm": gbs / hbm, "kernel_launches": launches, "note": note}
+
+    if c5 is not None:
+        # C5 LM head [2048, 2048] x [2048, 151936] and its acceptance, on the step's last state
+        hid, w_out, logits, keys = c5["hidden"], c5["w_out"], c5["logits"], c5["keys"]
+        tk, pa, nn, uni = c5["tree"]
+        Bc, Nc = tk.shape
+        lmws = a11spec.ops.workspace(256, dev)
+        flops = 2.0 * hid.shape[0] * hid.shape[1] * w_out.shape[0]
+        us = device_time_us(lambda i: a11spec.lm_head(hid, w_out, out=logits, keys=keys, ws=lmws), 10)
+        tf = flops / (us * 1e-6) / 1e12
+        out["C5_lm_head"] = {"us_per_launch": us, "flops_per_launch": flops, "achieved_tflops": tf,
+                             "frac_tensor_burst": tf / pk["tflops"], "bound": "tensor", "kernel_launches": 1,
+                             "note": "logits and the chunk keys of the acceptance (tcgen05, TMA stores)"}
+        # cuBLAS on the same product, for comparison (not on the step's path): the faster of the
+        # weight as stored ([vocab, hidden], F.linear) and a [hidden, vocab] copy (torch.matmul)
+        us_nt = device_time_us(lambda i: torch.nn.functional.linear(hid, w_out, out=logits), 4)
+        w_hv = w_out.t().contiguous()
+        us_nn = device_time_us(lambda i: torch.matmul(hid, w_hv, out=logits), 10)
+        del w_hv
+        us = min(us_nt, us_nn)
+        tf = flops / (us * 1e-6) / 1e12
+        out["C5_lm_head_cublas"] = {"us_per_launch": us, "achieved_tflops": tf, "frac_tensor_burst": tf / pk["tflops"],
+                                    "us_weight_as_stored": us_nt, "us_weight_transposed_copy": us_nn,
+                                    "note": "the same product by cuBLAS, for comparison; not on the step's path"}
+        a11spec.lm_head(hid, w_out, out=logits, keys=keys, ws=lmws)  # the keys of these logits
+        lg3 = logits.view(Bc, Nc, -1)
+        acc = a11spec.ops.alloc_accept(a11spec.STOCH_ONEHOT, Bc, Nc, lg3.shape[2], dev)
+        us = device_time_us(lambda i: a11spec.accept(a11spec.STOCH_ONEHOT, lg3, tk, pa, nn, temperature=TEMP,
+                                                     uniforms=uni, out=acc), 10)
+        out["C5_accept_stream"] = hbm_entry(us, lg3.numel() * 2, 2,
+                                            "a11s_accept over the 622 MB of logits (record init + accept "
+                                            "kernel): the pass the step replaces with the LM head's keys")
+        us = device_time_us(lambda i: a11spec.accept(a11spec.STOCH_ONEHOT, lg3, tk, pa, nn, temperature=TEMP,
+                                                     uniforms=uni, out=acc, keys=keys), 10)
+        out["C5_accept_recorded"] = {"us_per_launch": us, "bound": "latency", "kernel_launches": 2,
+                                     "mean_accept_len": float(acc.accept_len.float().mean()),
+                                     "note": "records from the LM head's keys (init) + the walk; reads the "
+                                             "visited rows only"}
+        del acc
 
     # C1: greedy chain, B=1, fp32 [6, 32000]: latency-bound
     d = W.make_c1(seed=1)
@@ -295,7 +338,10 @@ def run_ours(args, rank, world, local_rank):
     host_copy = None
     if world == 1 and not args.no_cpu_baseline:
         host_copy = host_state(st)  # before the step changes the page tables and lengths
-    table, q, hidden, w = st["table"], st["q"], st["hidden"], st["w"]
+    table, q, hidden = st["table"], st["q"], st["hidden"]
+    # the output projection as a model stores it, [vocab, hidden] (output_w of engine/pipeline.py:470)
+    w_out = st["w"].t().contiguous()
+    del st["w"]
     k_pool, v_pool = st["k_pool"], st["v_pool"]
     page_table, ctx_lens = st["page_table"], st["ctx_lens"]
     # the device page allocator owns every page no context holds; each step
@@ -315,9 +361,11 @@ def run_ours(args, rank, world, local_rank):
     attn_out = torch.empty_like(q)
     attn_ws = a11spec.ops.workspace(a11spec.ops.tree_attention_workspace_bytes(B, MAX_NODES, HQ, HKV, D, max_kv), dev)
     # liba11spec kernels per step: n-gram expand, page reserve, tree attention (+ split combine),
-    # accept (record init + accept), compaction (2), page release, next roots
-    launches_per_step = 9 + (1 if attn_ws.numel() > 256 else 0)
+    # LM head, accept (records from the head's keys + accept), compaction (2), page release, next roots
+    launches_per_step = 10 + (1 if attn_ws.numel() > 256 else 0)
     logits = torch.empty(B * MAX_NODES, VOCAB, dtype=torch.bfloat16, device=dev)
+    keys = torch.empty(B * MAX_NODES, (VOCAB + 2047) // 2048, dtype=torch.int64, device=dev)
+    lmh_ws = a11spec.ops.workspace(256, dev)
     uni = torch.empty(B, MAX_NODES, dtype=torch.float32, device=dev)
     acc = a11spec.ops.alloc_accept(a11spec.STOCH_ONEHOT, B, MAX_NODES, VOCAB, dev)
     freed = torch.full_like(page_table, -1)
@@ -351,7 +399,7 @@ def run_ours(args, rank, world, local_rank):
         pages.reserve(page_table, grown, nn)  # pages for the tree slots ctx_lens + i
         evs = None
         if timed_events is not None:
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(6)]
             evs[0].record()
         wait(1)
         a11spec.tree_attention(qq, k_pool, v_pool, page_table, ctx_lens, pa, nn, max_kv_len=max_kv,
@@ -359,7 +407,12 @@ def run_ours(args, rank, world, local_rank):
         if evs:
             evs[1].record()
         wait(2)
-        torch.matmul(hid, w, out=logits)
+        if evs:
+            evs[4].record()
+        # K7: logits and the acceptance's chunk keys in one tcgen05 GEMM
+        a11spec.lm_head(hid, w_out, out=logits, keys=keys, ws=lmh_ws)
+        if evs:
+            evs[5].record()
         wait(3)
         if un is None:
             uni.uniform_(generator=gen)
@@ -369,7 +422,7 @@ def run_ours(args, rank, world, local_rank):
         if evs:
             evs[2].record()
         a11spec.accept(a11spec.STOCH_ONEHOT, logits.view(B, MAX_NODES, VOCAB), tk, pa, nn,
-                       temperature=TEMP, uniforms=un, stats=stats, out=acc)
+                       temperature=TEMP, uniforms=un, stats=stats, out=acc, keys=keys)
         if evs:
             evs[3].record()
             timed_events.append(evs)
@@ -401,6 +454,7 @@ def run_ours(args, rank, world, local_rank):
     emitted = int((stats - s0)[STAT_NAMES.index("emitted_tokens")])
     attn_ms = sum(e[0].elapsed_time(e[1]) for e in ev_kernels) / len(ev_kernels)
     acc_ms = sum(e[2].elapsed_time(e[3]) for e in ev_kernels) / len(ev_kernels)
+    lmh_ms = sum(e[4].elapsed_time(e[5]) for e in ev_kernels) / len(ev_kernels)
 
     # end to end through the public API with host buffers: pinned H2D of the
     # step's inputs (hidden states, queries, uniforms, last tokens) and D2H of
@@ -473,20 +527,20 @@ def run_ours(args, rank, world, local_rank):
 
     reducer.finish()
     torch.cuda.synchronize()
-    t = torch.tensor([ms, e2e_ms, attn_ms, acc_ms], dtype=torch.float64, device=dev)
+    t = torch.tensor([ms, e2e_ms, attn_ms, acc_ms, lmh_ms], dtype=torch.float64, device=dev)
     cnt = torch.tensor([emitted, e2e_emitted], dtype=torch.int64, device=dev)
     if world > 1:
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
         torch.distributed.all_reduce(cnt, op=torch.distributed.ReduceOp.SUM)
-    ms, e2e_ms, attn_ms, acc_ms = (float(x) for x in t.tolist())
+    ms, e2e_ms, attn_ms, acc_ms, lmh_ms = (float(x) for x in t.tolist())
     emitted, e2e_emitted = (int(x) for x in cnt.tolist())
     if rank != 0:
         return None
     pk = peaks()
     attn_flops = 4.0 * B * HQ * MAX_NODES * (CTX + MAX_NODES / 2) * D  # per launch, tree half-masked
     attn_tflops = attn_flops / (attn_ms * 1e-3) / 1e12
-    acc_bytes = B * MAX_NODES * VOCAB * 2
-    acc_gbs = acc_bytes / (acc_ms * 1e-3) / 1e9
+    lmh_flops = 2.0 * B * MAX_NODES * HIDDEN * VOCAB
+    lmh_tflops = lmh_flops / (lmh_ms * 1e-3) / 1e12
     line = {
         "metric": METRIC, "value": emitted / (ms * 1e-3), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -494,16 +548,16 @@ def run_ours(args, rank, world, local_rank):
         "data": "synthetic (seeded; no dataset exists for this path)",
         "config": workload_config(world),
         "mean_emitted_per_seq": emitted / (args.steps * B * world),
-        "kernel_us": {"tree_attention": attn_ms * 1e3, "accept": acc_ms * 1e3},
+        "kernel_us": {"tree_attention": attn_ms * 1e3, "lm_head": lmh_ms * 1e3, "accept": acc_ms * 1e3},
         # the timed region is tens of milliseconds, so the burst GEMM peak is the denominator
         "roofline": {"kernel": "tree_attention", "bound": "tensor", "achieved": attn_tflops,
                      "peak": pk["tflops"], "unit": "TFLOP/s", "frac": attn_tflops / pk["tflops"],
                      "peak_source": f"{pk['src']} bf16 burst", "frac_of_sustained": attn_tflops / pk["tflops_sus"],
                      "traffic": profile_traffic("tree_attention_c5"), "flops_per_launch": attn_flops},
-        "roofline_accept": {"kernel": "accept (one-hot sampling, T=0.7)", "bound": "hbm", "achieved": acc_gbs,
-                            "peak": pk["hbm"], "unit": "GB/s", "frac": acc_gbs / pk["hbm"],
-                            "peak_source": f"{pk['src']} HBM copy", "bytes_per_launch": acc_bytes,
-                            "us_includes": "record init + accept kernel"},
+        "roofline_lm_head": {"kernel": "lm_head (chunk keys in the epilogue)", "bound": "tensor",
+                             "achieved": lmh_tflops, "peak": pk["tflops"], "unit": "TFLOP/s",
+                             "frac": lmh_tflops / pk["tflops"], "peak_source": f"{pk['src']} bf16 burst",
+                             "flops_per_launch": lmh_flops},
         "e2e": {"value": e2e_emitted / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo},
         "gpu_launches": args.steps * launches_per_step,
@@ -512,7 +566,16 @@ def run_ours(args, rank, world, local_rank):
     if reducer.result() is not None:
         line["acceptance_stats_global"] = reducer.result()
     if world == 1 and not args.no_configs:
-        line["configs"] = measure_configs(dev, pk)
+        cfg = measure_configs(dev, pk, dict(hidden=hidden, w_out=w_out, logits=logits, keys=keys,
+                                            tree=(tree[0], tree[1], tree[3], uni)))
+        line["configs"] = cfg
+        st_ = cfg["C5_accept_stream"]
+        line["roofline_accept"] = {"kernel": "accept over the logits (one-hot sampling, T=0.7)", "bound": "hbm",
+                                   "achieved": st_["achieved_gbs"], "peak": pk["hbm"], "unit": "GB/s",
+                                   "frac": st_["frac_hbm"], "peak_source": f"{pk['src']} HBM copy",
+                                   "bytes_per_launch": st_["bytes_per_launch"],
+                                   "us_includes": "record init + accept kernel",
+                                   "on_step_path": False}
     if host_copy is not None:
         line["cpu_baseline"] = cpu_baseline(host_copy)
     return line
