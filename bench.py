@@ -223,7 +223,7 @@ def measure_configs(dev, pk, c5=None) -> dict:
                              "note": "logits and the chunk keys of the acceptance (tcgen05, TMA stores)"}
         # cuBLAS on the same product, for comparison (not on the step's path): the faster of the
         # weight as stored ([vocab, hidden], F.linear) and a [hidden, vocab] copy (torch.matmul)
-        us_nt = device_time_us(lambda i: torch.nn.functional.linear(hid, w_out, out=logits), 4)
+        us_nt = device_time_us(lambda i: torch.nn.functional.linear(hid, w_out), 4)
         w_hv = w_out.t().contiguous()
         us_nn = device_time_us(lambda i: torch.matmul(hid, w_hv, out=logits), 10)
         del w_hv
