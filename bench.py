@@ -557,7 +557,9 @@ def run_ours(args, rank, world, local_rank):
         "roofline_lm_head": {"kernel": "lm_head (chunk keys in the epilogue)", "bound": "tensor",
                              "achieved": lmh_tflops, "peak": pk["tflops"], "unit": "TFLOP/s",
                              "frac": lmh_tflops / pk["tflops"], "peak_source": f"{pk['src']} bf16 burst",
-                             "flops_per_launch": lmh_flops},
+                             "flops_per_launch": lmh_flops,
+                             "traffic_small_case": profile_traffic("lm_head_small"),
+                             "traffic_case": "2048 x 2048 x 32768 (weight larger than L2), profiles/lm_head_c5.md"},
         "e2e": {"value": e2e_emitted / (e2e_ms * 1e-3), "unit": UNIT, "h2d_bytes_per_step": bi,
                 "d2h_bytes_per_step": bo},
         "gpu_launches": args.steps * launches_per_step,

@@ -5,6 +5,7 @@
     python bench_cases.py compact --batch 32 --ctx 4096 --iters 2
     python bench_cases.py ngram --batch 32 --iters 2
     python bench_cases.py pages --batch 32 --ctx 32768 --iters 20
+    python bench_cases.py lm_head --batch 32 --nodes 64 --vocab 32768 --iters 2
 
 Each case builds its inputs on cuda:0 (seeded), runs the kernel `--warmup`
 times, then `--iters` times between CUDA events, and prints one JSON line
@@ -194,19 +195,38 @@ def case_ngram_update(a) -> dict:
     return {"case": "ngram_update", "batch": B, "us": us, "trigrams": int(status[1])}
 
 
+def case_lm_head(a) -> dict:
+    """The tree nodes' LM head: `batch` x `nodes` rows of hidden size `hidden`
+    against a [vocab, hidden] output projection, with the chunk keys."""
+    dev = "cuda"
+    g = torch.Generator(device=dev).manual_seed(6)
+    R, H, V = a.batch * a.nodes, a.hidden, a.vocab
+    h = torch.randn(R, H, device=dev, generator=g).to(torch.bfloat16)
+    w = (torch.randn(V, H, device=dev, generator=g) / H ** 0.5).to(torch.bfloat16)
+    out = torch.empty(R, V, dtype=torch.bfloat16, device=dev)
+    keys = torch.empty(R, (V + 2047) // 2048, dtype=torch.int64, device=dev)
+    ws = a11spec.ops.workspace(256, dev)
+    us = _time(lambda: a11spec.lm_head(h, w, out=out, keys=keys, ws=ws), a.warmup, a.iters)
+    flops = 2.0 * R * H * V
+    return {"case": "lm_head", "rows": R, "hidden": H, "vocab": V, "us": us, "flops": flops,
+            "tflops": flops / us / 1e6, "bytes": 2 * (R * H + V * H + R * V)}
+
+
 def main(argv=None) -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
-    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram", "pages", "ngram_update"])
+    ap.add_argument("case", choices=["attention", "accept", "compact", "ngram", "pages", "ngram_update", "lm_head"])
     ap.add_argument("--batch", type=int, default=16)
     ap.add_argument("--ctx", type=int, default=4096)
     ap.add_argument("--nodes", type=int, default=64)
     ap.add_argument("--mode", choices=["greedy", "onehot", "draft", "c4greedy"], default="greedy")
+    ap.add_argument("--hidden", type=int, default=2048)
+    ap.add_argument("--vocab", type=int, default=VOCAB)
     ap.add_argument("--warmup", type=int, default=1)
     ap.add_argument("--iters", type=int, default=2)
     a = ap.parse_args(argv)
     torch.cuda.set_device(0)
     fn = {"attention": case_attention, "accept": case_accept, "compact": case_compact, "ngram": case_ngram,
-          "pages": case_pages, "ngram_update": case_ngram_update}[a.case]
+          "pages": case_pages, "ngram_update": case_ngram_update, "lm_head": case_lm_head}[a.case]
     print(json.dumps(fn(a)), flush=True)
 
 
