@@ -106,8 +106,11 @@ class SpeculativeDecoder:
         return DraftTree(tk, pa, de, nn)
 
     def verify(self, tree: DraftTree, target_logits: torch.Tensor, uniforms: Optional[torch.Tensor] = None,
-               draft_logits: Optional[torch.Tensor] = None, out: Optional[ops.AcceptResult] = None):
-        """K3 on [B, N, V] logits (row i judges node i's children)."""
+               draft_logits: Optional[torch.Tensor] = None, out: Optional[ops.AcceptResult] = None,
+               keys: Optional[torch.Tensor] = None):
+        """K3 on [B, N, V] logits (row i judges node i's children). keys: the
+        chunk keys a11s_lm_head wrote with these bf16 logits; the acceptance
+        then takes its records from them (not with draft logits)."""
         if self.temperature is None:
             mode = _lib.GREEDY
         else:
@@ -115,9 +118,11 @@ class SpeculativeDecoder:
             if uniforms is None:
                 B, N = tree.tokens.shape
                 uniforms = torch.rand(B, N, generator=self._gen, device=self.device)
+        if draft_logits is not None or target_logits.dtype != torch.bfloat16:
+            keys = None
         return ops.accept(mode, target_logits, tree.tokens, tree.parents, tree.n_nodes,
                           draft_logits=draft_logits, temperature=self.temperature or 1.0,
-                          uniforms=uniforms, stats=self.stats, out=out)
+                          uniforms=uniforms, stats=self.stats, out=out, keys=keys)
 
     def step(self, last_tokens: torch.Tensor, q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
              page_table: torch.Tensor, seq_lens: torch.Tensor,

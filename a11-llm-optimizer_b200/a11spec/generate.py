@@ -69,7 +69,9 @@ def speculative_stream(model, prompts: torch.Tensor, max_new_tokens: int, decode
         pages.reserve(page_table, grown, tree.n_nodes)
         logits = model.forward_tree(tree.tokens, tree.parents, tree.n_nodes, page_table, ctx_lens)
         uni = uniforms_fn(B, N) if (uniforms_fn is not None and decoder.temperature is not None) else None
-        res = decoder.verify(tree, logits, uniforms=uni)  # draws its own uniforms when sampling without them
+        # draws its own uniforms when sampling without them; takes its records from
+        # the LM head's chunk keys when the model's head left them
+        res = decoder.verify(tree, logits, uniforms=uni, keys=getattr(model, "last_chunk_keys", None))
         freed, n_freed = ops.kv_compact(model.k_pool, model.v_pool, page_table, ctx_lens, res.accept_len,
                                         res.accepted_nodes, tree.n_nodes,
                                         num_layers=getattr(model, "num_layers", 1))

@@ -110,6 +110,7 @@ class TreeDecoder:
         self.k_pool = torch.zeros(shape, dtype=torch.bfloat16, device=self.device)
         self.v_pool = torch.zeros_like(self.k_pool)
         self.forwards = 0
+        self.last_chunk_keys = None  # chunk keys of the last forward's logits (K7), or None
 
     def _proj(self, x: torch.Tensor, name: str) -> torch.Tensor:
         y = torch.matmul(x, self.w[name + ".weight"].t())
@@ -152,7 +153,21 @@ class TreeDecoder:
             h = h + self._proj(act, blk + "ffn_down")
         hn = rms_norm(h, self.w["output_norm.weight"], cfg.rms_eps)
         self.forwards += 1
-        return self._proj(hn, "output")
+        return self._head(hn)
+
+    def _head(self, hn: torch.Tensor) -> torch.Tensor:
+        """logits = hn output_w^T (engine/pipeline.py:469-472). A bf16 model
+        whose sizes K7 takes (multiples of 8) runs a11s_lm_head, which also
+        leaves the acceptance's chunk keys in last_chunk_keys; otherwise torch."""
+        w = self.w["output.weight"]
+        V, H = w.shape
+        self.last_chunk_keys = None
+        if w.dtype != torch.bfloat16 or H % 8 or V % 8 or "output.bias" in self.w:
+            return self._proj(hn, "output")
+        lead = hn.shape[:-1]
+        logits, keys, _ = ops.lm_head(hn.reshape(-1, H).to(torch.bfloat16).contiguous(), w, want_keys=True)
+        self.last_chunk_keys = keys
+        return logits.view(*lead, V)
 
     # -- the target-model interface of generate.speculative_stream -----------
     def forward_tree(self, tokens, parents, n_nodes, page_table, ctx_lens) -> torch.Tensor:
