@@ -816,6 +816,12 @@ template <int MODE, bool BF16>
 __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a) {
     const int b = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     __shared__ double s_invT[MODE == A11S_ACCEPT_GREEDY ? 1 : kWarps][A11S_MAX_WALK_LEVELS + 1];
+    // The launch may overlap the record-init kernel before it (programmatic
+    // dependent launch): everything it writes (status, counters, records, pass
+    // area) is touched only after this wait, which returns once that kernel
+    // has completed and its writes are visible. Without such a launch it
+    // returns at once.
+    asm volatile("griddepcontrol.wait;" ::: "memory");
     if ((int)blockIdx.y >= a.bulk_rows) {  // helper block (sampling modes only)
         if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, true, s_invT[warp]);
         return;
@@ -830,17 +836,18 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // root in DRAFT mode), then the other rows in index order (in DRAFT mode
     // p row i then q row i), a row's chunks consecutive, so the rows near the
     // root, which the walk visits first, are recorded first. Grid row 0 is the
-    // sequence's walker; in the sampling modes it streams nothing and rows 1 ..
-    // root_blocks take the root units (chunk maxima and weight sums), one per
-    // warp, so every root is recorded in the first wave by many SMs at once;
-    // in GREEDY the walker records its root itself (root_blocks = 0). The rows
-    // after them take the other units in slices.
+    // sequence's walker and streams nothing; rows 1 .. root_blocks take the
+    // root units (chunk maxima, and first positions in GREEDY or weight sums in
+    // the sampling modes), one per warp, so every root is recorded in the first
+    // wave by many SMs at once. (root_blocks = 0 only in GREEDY with chunk
+    // keys, whose records are all written before the launch.) The rows after
+    // them take the other units in slices.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
     int u0 = 0, u1 = 0;
     if (blockIdx.y == 0 && a.root_blocks == 0) {
-        // GREEDY: the walker records its root itself (maxima only, cheap);
-        // with chunk keys every record is written before the launch
+        // without root blocks the walker records its root itself; with chunk
+        // keys every record is written before the launch
         u1 = a.keys ? 0 : n_root_units;
     } else if (blockIdx.y >= 1 && (int)blockIdx.y <= a.root_blocks) {
         u0 = (blockIdx.y - 1) * kWarps;
@@ -1377,6 +1384,9 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
 // Before every acceptance launch: clear the status word and set every record
 // to kUnrecorded (one launch instead of two memsets).
 __global__ void accept_init_kernel(StatusWord *st, uint4 *recs, size_t n16, uint4 *zero, size_t z16) {
+    // the acceptance kernel after this one may be scheduled now: it waits for
+    // this grid's completion before it reads anything written here
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
     const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i0 == 0) {
         *st = StatusWord{};
@@ -1398,6 +1408,7 @@ cudaError_t launch_accept_init(StatusWord *st, void *recs, size_t bytes, void *z
 }
 
 __global__ void accept_keys_init_kernel(const AcceptArgs a, int mode, uint4 *zero, size_t z16) {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");  // as in accept_init_kernel
     const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
     if (i0 == 0) {
         *a.status = StatusWord{};
@@ -1437,12 +1448,20 @@ cudaError_t launch_accept_keys_init(int mode, const AcceptArgs &a, void *zero, s
 }
 
 cudaError_t launch_accept(int mode, bool bf16, const AcceptArgs &a, int grid_y, cudaStream_t s) {
-    dim3 grid(a.B, grid_y), block(kThreads);  // sequences fastest: every root block in the first wave
+    // sequences fastest: every root block in the first wave; launched as a
+    // programmatic dependent of the record-init kernel queued just before it
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(a.B, grid_y);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
 #define A11S_LAUNCH(M, BF)                                                   \
-    if (mode == M && bf16 == BF) {                                           \
-        accept_kernel<M, BF><<<grid, block, 0, s>>>(a);                      \
-        return cudaGetLastError();                                           \
-    }
+    if (mode == M && bf16 == BF) return cudaLaunchKernelEx(&cfg, accept_kernel<M, BF>, a);
     A11S_LAUNCH(A11S_ACCEPT_GREEDY, false)
     A11S_LAUNCH(A11S_ACCEPT_GREEDY, true)
     A11S_LAUNCH(A11S_ACCEPT_STOCH_ONEHOT, false)

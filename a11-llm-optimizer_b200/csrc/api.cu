@@ -182,14 +182,15 @@ int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const vo
     // half of the 2 resident blocks per SM: the bulk pass always has room.
     a.wait_records = batch <= sm_count() ? 1 : 0;
 
-    // Grid row 0 of a sequence walks its tree; in the sampling modes it streams
-    // nothing and rows 1 .. root_blocks take its root rows' units (maxima and
-    // weight sums), one per warp, so every root is recorded in the first wave;
-    // in GREEDY the walker records its root itself. The other units are balanced over about 4
-    // waves of 2 resident 512-thread blocks per SM, at least 16 chunks (one
-    // per warp) per block.
+    // Grid row 0 of a sequence walks its tree and streams nothing; rows 1 ..
+    // root_blocks take its root rows' units (maxima, first positions in GREEDY,
+    // weight sums in the sampling modes), one per warp, so every root is
+    // recorded in the first wave by many SMs at once. With chunk keys GREEDY
+    // needs no root blocks: every record is written before the launch. The
+    // other units are balanced over about 4 waves of 2 resident 512-thread
+    // blocks per SM, at least 16 chunks (one per warp) per block.
     const int root_units = a.nch * (mode == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1);
-    a.root_blocks = mode == A11S_ACCEPT_GREEDY ? 0 : (root_units + 15) / 16;
+    a.root_blocks = (mode == A11S_ACCEPT_GREEDY && keys) ? 0 : (root_units + 15) / 16;
     a.keys = reinterpret_cast<const unsigned long long *>(keys);
     const long long rest = (long long)a.units_per_seq - root_units;
     const long long target_blocks = (long long)sm_count() * 2 * 4;
