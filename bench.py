@@ -102,7 +102,7 @@ def workload_config(world: int) -> dict:
             "seqs_per_gpu": B_PER_GPU, "global_seqs": B_PER_GPU * world, "ctx": CTX, "max_nodes": MAX_NODES,
             "gqa": f"{HQ}/{HKV}", "head_dim": D, "vocab": VOCAB, "temperature": TEMP,
             "parallelism": f"request-batch dp{world}",
-            "l2": "inputs larger than L2 (2.15 GB KV + 622 MB logits per step)"}
+            "l2": "inputs larger than L2 (2.15 GB KV, 622 MB LM-head weight and 622 MB logits per step)"}
 
 
 def gpu_id(dev) -> str:
