@@ -173,6 +173,19 @@ def test_recorded_accept_matches_accept(dev, head_weight, mode):
     assert int(r.accept_len.max()) >= 2  # the walks leave the root
 
 
+@pytest.mark.parametrize("mode", [_lib.GREEDY, _lib.STOCH_ONEHOT])
+def test_recorded_accept_ragged_trees(dev, head_weight, mode):
+    """Sequences with fewer live nodes than max_nodes: the dead rows' keys (of
+    whatever the head computed for them) take no part, as their logits do not
+    in a11s_accept."""
+    B, N = 12, 24
+    h, parents, tokens, _ = _tree_batch(head_weight, B, N, seed=31 + mode)
+    n_nodes = torch.tensor([N if b % 3 == 0 else 1 + (7 * b) % N for b in range(B)], dtype=torch.int32,
+                           device="cuda")
+    lg, keys, _ = ops.lm_head(h, head_weight, want_keys=True)
+    _accept_both(mode, lg.view(B, N, V5), keys, tokens, parents, n_nodes, temperature=0.7, seed=5)
+
+
 def test_recorded_accept_c5_shape(dev, head_weight):
     """The bench's acceptance: one-hot drafts at T = 0.7 on [32, 64, 151936] bf16 logits."""
     B, N = 32, 64
