@@ -10,7 +10,7 @@
 // One CTA = one sequence b, one KV head g, 32 tree nodes x 8 query heads as
 // two Q tiles of 128 rows (the MMA M), one split of the KV range. 384 threads:
 //   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane;
-//              at the start each thread copies its Q row into TMEM
+//              at the start each thread copies its Q row into shared memory
 //   warp 8     TMA producer: K and V blocks of 128 keys (8 pages, one 64x16
 //              box per page and 64-column half) into a 3-slot K ring and a
 //              2-slot V ring shared by both tiles; page ids fetched 4 blocks
@@ -19,16 +19,16 @@
 //   warp 11    PV issuer
 //   warp 10    idle (completes the third warpgroup for the register split:
 //              softmax warps 216 registers, warps 8-11 56)
+// Shared memory: Q of each tile (the A operand of QK^T), the K and V rings.
 // TMEM (512 columns): one S buffer of 128 columns used by the tiles in turn,
-// O of each tile (128 dims), Q of each tile as bf16 pairs (64 columns).
-// Per block j and tile t: S = Q_t K_j^T (8 x tcgen05.mma M128 N128 K16, A = Q
-// from TMEM, K a K-major shared-memory operand). The softmax warps load S
-// into registers and release the buffer at once (the other tile's S is
-// computed into it meanwhile), mask it (ancestor bits), exponentiate (one
-// packed FFMA per pair of scores, one ex2 each), keep fp32 row sums of the
-// unrounded values and store P_t rounded to bf16 (nearest even) into shared
-// memory in the 128-byte-swizzled K-major layout; then O_t += P_t V_j (8 MMAs,
-// A = P from shared memory, V an MN-major shared-memory operand).
+// O of each tile (128 dims), P of each tile as bf16 pairs (64 columns).
+// Per block j and tile t: S = Q_t K_j^T (8 x tcgen05.mma M128 N128 K16, Q and
+// K K-major shared-memory operands). The softmax warps load S into registers
+// and release the buffer at once (the other tile's S is computed into it
+// meanwhile), mask it (ancestor bits), exponentiate (one packed FFMA per pair
+// of scores, one ex2 each), keep fp32 row sums of the unrounded values and
+// store P_t rounded to bf16 (nearest even) into its TMEM columns; then
+// O_t += P_t V_j (8 MMAs, A = P from TMEM, V an MN-major shared-memory operand).
 // Two issuer threads: a thread's next shared-memory access (an mbarrier
 // poll) waits until the tensor core has read its MMAs' shared-memory
 // operands, so one thread issuing both kinds of group leaves the tensor pipe
@@ -36,8 +36,11 @@
 // while the other's group executes.
 // Why this shape: an M128 N64 K16 MMA costs about 58 cycles whatever its
 // operands, against 32 of math, while N = 128 runs at its math rate; P in
-// shared memory lets S(j+1) overwrite the S buffer while P(j) waits for PV,
-// instead of PV(j) having to finish first.
+// columns of its own lets S(j+1) overwrite the S buffer while P(j) waits for
+// PV, instead of PV(j) having to finish first. With Q in shared memory and P
+// in TMEM a block moves about 256 KB through shared memory (TMA writes 64, QK^T
+// reads 128, PV reads 64) instead of 320 KB with P in shared memory and Q in
+// TMEM.
 // The running max is updated lazily: O and l are rescaled only when the block
 // max exceeds the reference max by more than 8 (log2 units), which keeps every
 // exponent <= 2^8. Split-KV partials are merged by tree_attn_combine.
@@ -67,17 +70,17 @@ constexpr int kProducerWarp = kSoftmaxWarps, kMmaWarp = kSoftmaxWarps + 1, kPvWa
 constexpr int kTcThreads = 32 * (kSoftmaxWarps + 4);  // + producer, 2 issuers, 1 idle: whole warpgroups
 constexpr int kRegsSoftmax = 216, kRegsOther = 56;    // setmaxnreg split (multiples of 8)
 constexpr long long kRegsNeeded = 32ll * (kSoftmaxWarps * kRegsSoftmax + 4 * kRegsOther);
-constexpr uint32_t kPHalf = 16384;    // P tile: 128 rows x 128 B per 64-key half
+constexpr uint32_t kQHalf = 16384;    // Q tile: 128 rows x 128 B per 64-dim half
 constexpr uint32_t kKVHalf = 16384;   // K or V: 128 tokens x 128 B per 64-dim half
-constexpr uint32_t kOffP = 0;                                // P of tile t at 2*kPHalf*t
+constexpr uint32_t kOffQ = 0;                                // Q of tile t at 2*kQHalf*t
 constexpr uint32_t kSlotBytes = 2 * kKVHalf;                 // one K or V block: 32 KB
-constexpr uint32_t kOffK = kTiles * 2 * kPHalf;              // K slots
+constexpr uint32_t kOffK = kTiles * 2 * kQHalf;              // K slots
 constexpr uint32_t kOffV = kOffK + kKStages * kSlotBytes;    // V slots
 constexpr uint32_t kOffBar = kOffV + kVStages * kSlotBytes;  // 229376
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
 // TMEM (512 columns): one S buffer shared by the tiles, O[tile], Q[tile] (bf16 pairs)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColS = 0, kColO = 128, kColQ = 384;
+constexpr uint32_t kColS = 0, kColO = 128, kColP = 384;  // P of tile t: 64 columns of bf16 pairs
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 constexpr float kRescaleThreshold = 8.0f;
 constexpr uint32_t kIdescS = tc::idesc_bf16_f32(128, kBlockKV, false);
@@ -329,11 +332,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else if (warp == kMmaWarp) {
             // ---------------- S issuer ----------------
             if (lane == 0) {
-                auto issue_s = [&](int j, int t) {  // S = Q_t K_j^T: 8 MMAs M128 N128 K16, A = Q from TMEM
+                auto issue_s = [&](int j, int t) {  // S = Q_t K_j^T: 8 MMAs M128 N128 K16, Q and K in shared memory
                     const uint32_t k_addr = tc::smem_u32(sm + kOffK + (j % kKStages) * kSlotBytes);
+                    const uint32_t q_addr = tc::smem_u32(sm + kOffQ + t * 2 * kQHalf);
     #pragma unroll
                     for (int kk = 0; kk < 8; ++kk)
-                        tc::mma_bf16_ts(tmem + kColS, tmem + kColQ + 64 * t + kk * 8,
+                        tc::mma_bf16_ss(tmem + kColS,
+                                        tc::sdesc_sw128(q_addr + (kk >> 2) * kQHalf + (kk & 3) * 32, 16, 1024),
                                         tc::sdesc_sw128(k_addr + (kk >> 2) * kKVHalf + (kk & 3) * 32, 16, 1024),
                                         kIdescS, kk > 0);
                     tc::mma_commit(&bs->s_full[t]);
@@ -359,13 +364,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         } else if (warp == kPvWarp) {
             // ---------------- PV issuer ----------------
             if (lane == 0) {
-                auto issue_pv = [&](int j, int t) {  // O_t += P_t V_j: 8 MMAs M128 N128 K16, A = P from shared memory
+                auto issue_pv = [&](int j, int t) {  // O_t += P_t V_j: 8 MMAs M128 N128 K16, A = P from TMEM
                     const uint32_t v_addr = tc::smem_u32(sm + kOffV + (j % kVStages) * kSlotBytes);
-                    const uint32_t p_addr = tc::smem_u32(sm + kOffP + t * 2 * kPHalf);
     #pragma unroll
                     for (int kk = 0; kk < kBlockKV / 16; ++kk)
-                        tc::mma_bf16_ss(tmem + kColO + 128 * t,
-                                        tc::sdesc_sw128(p_addr + (kk >> 2) * kPHalf + (kk & 3) * 32, 16, 1024),
+                        tc::mma_bf16_ts(tmem + kColO + 128 * t, tmem + kColP + 64 * t + kk * 8,
                                         tc::sdesc_sw128(v_addr + kk * 2048, kKVHalf, 1024), kIdescPV,
                                         (j > 0 || kk > 0) ? 1u : 0u);
                     tc::mma_commit(&bs->pv_done[t]);
@@ -393,33 +396,24 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         // lane = row): 256 bytes, zeros past the last node. The issuer
         // waits for q_ready before the first S.
         {
-            uint32_t qv[64];
-            if (node < p.N) {
-                const uint4 *src = reinterpret_cast<const uint4 *>(p.q + (((size_t)b * p.N + node) * p.Hq + row_head) * 128);
+            // 256 bytes of Q into the tile's 128-byte-swizzled K-major A operand:
+            // 64-dim half h at 16 KB h, row m at 128 m, 16-byte chunk c at slot c ^ (m & 7)
+            const uint32_t q_row = tc::smem_u32(sm + kOffQ + tile * 2 * kQHalf + m * 128);
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.q + (((size_t)b * p.N + node) * p.Hq + row_head) * 128);
 #pragma unroll
-                for (int c = 0; c < 16; ++c) {
-                    const uint4 v = __ldg(src + c);
-                    qv[4 * c] = v.x;
-                    qv[4 * c + 1] = v.y;
-                    qv[4 * c + 2] = v.z;
-                    qv[4 * c + 3] = v.w;
-                }
-            } else {
-#pragma unroll
-                for (int c = 0; c < 64; ++c) qv[c] = 0u;
+            for (int c = 0; c < 16; ++c) {
+                const uint4 v = node < p.N ? __ldg(src + c) : make_uint4(0, 0, 0, 0);
+                const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+                tc::st_shared_v4(q_row + (uint32_t)(c >> 3) * kQHalf + ((uint32_t)((c & 7) ^ (m & 7)) << 4), w);
             }
-            tc::tmem_st32u(tmem + lane_base + kColQ + 64 * tile, qv);
-            tc::tmem_st32u(tmem + lane_base + kColQ + 64 * tile + 32, qv + 32);
-            tc::tmem_wait_st();
-            tc::tc_fence_before();
+            tc::fence_proxy_async_smem();  // Q visible to the tensor core
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bs->q_ready);
         }
         // `ok` stays warp-uniform for the .sync.aligned TMEM accesses.
         const bool live = node < n_live;
         const uint64_t anc = bs->anc[node - node0];
-        // this row of P_t; XOR-ing 16-byte slot numbers into it gives the 128-byte swizzle
-        const uint32_t p_row = (tc::smem_u32(sm + kOffP + tile * 2 * kPHalf + m * 128)) ^ (uint32_t)((m & 7) << 4);
+        const uint32_t p_cols = tmem + lane_base + kColP + 64 * tile;  // this row of P_t (bf16 pairs)
         const float sl2 = p.scale_log2;
         float m_ref = -INFINITY, lsum = 0.0f;
         bool ok = true;
@@ -478,21 +472,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                 tc::tc_fence_after();
             }
             float2 ls[4] = {{0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}, {0.f, 0.f}};  // independent partial sums
-            // P as bf16 pairs (lower key in the low half), 16 bytes per 8 keys:
-            // chunk c of the row goes to 16-byte slot c ^ (row & 7) of its
-            // 64-key half (the 128-byte swizzle of a K-major operand).
+            // P as bf16 pairs (lower key in the low half) into the tile's P columns,
+            // 32 keys per store: the A operand of PV from TMEM
 #pragma unroll
-            for (int c8 = 0; c8 < kBlockKV / 8; ++c8) {
-                uint32_t pw[4];
+            for (int c32 = 0; c32 < kBlockKV / 32; ++c32) {
+                uint32_t pw[16];
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float2 ev = tc::ffma2(make_float2(X(8 * c8 + 2 * e), X(8 * c8 + 2 * e + 1)),
-                                                make_float2(sl2, sl2), make_float2(neg, neg));
+                for (int e = 0; e < 16; ++e) {
+                    const int c = 32 * c32 + 2 * e;
+                    const float2 ev = tc::ffma2(make_float2(X(c), X(c + 1)), make_float2(sl2, sl2), make_float2(neg, neg));
                     const float2 a = make_float2(tc::ex2(ev.x), tc::ex2(ev.y));
                     pw[e] = tc::cvt_bf16x2(a.x, a.y);
-                    ls[e] = tc::fadd2(ls[e], a);  // fp32 denominator of the unrounded p
+                    ls[e & 3] = tc::fadd2(ls[e & 3], a);  // fp32 denominator of the unrounded p
                 }
-                tc::st_shared_v4((p_row + (uint32_t)(c8 >> 3) * kPHalf) ^ (uint32_t)((c8 & 7) << 4), pw);
+                tc::tmem_st16u_nowait(p_cols + 16 * c32, pw);
             }
             lsum = lsum * alpha + (((ls[0].x + ls[0].y) + (ls[1].x + ls[1].y)) + ((ls[2].x + ls[2].y) + (ls[3].x + ls[3].y)));
             // Rescale O before PV(it) may start (the scores are dead by now).
@@ -506,7 +499,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                     tc::tmem_st32(tmem + lane_base + kColO + 128 * tile + c * 32, o);
                 }
             }
-            tc::fence_proxy_async_smem();  // P visible to the tensor core
+            tc::tmem_wait_st();  // P (and a rescaled O) written before PV(it) may read them
             tc::tc_fence_before();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&bs->p_full[tile]);
