@@ -12,8 +12,8 @@
 //   warps 0-7  softmax: warp w serves tile w/4, thread = query row = TMEM lane;
 //              at the start each thread copies its Q row into shared memory
 //   warp 8     TMA producer: K and V blocks of 128 keys (8 pages, one 64x16
-//              box per page and 64-column half) into a 3-slot K ring and a
-//              2-slot V ring shared by both tiles; page ids fetched 4 blocks
+//              box per page and 64-column half) into a 2-slot K ring and a
+//              3-slot V ring shared by both tiles; page ids fetched 4 blocks
 //              ahead
 //   warp 9     TMEM allocator + S issuer (QK^T groups)
 //   warp 11    PV issuer
@@ -60,8 +60,8 @@ namespace a11s {
 namespace {
 constexpr int kBlockKV = 128;         // keys per KV block = 8 pages (the N of the QK^T MMA)
 constexpr int kPagesPerBlock = kBlockKV / A11S_PAGE_TOKENS;
-constexpr int kKStages = 3;           // K ring depth: a K slot is free once QK^T of both tiles completed
-constexpr int kVStages = 2;           // V ring depth: a V slot is free once PV of both tiles completed
+constexpr int kKStages = 2;           // K ring depth: a K slot is free once QK^T of both tiles completed
+constexpr int kVStages = 3;           // V ring depth: a V slot is free once PV of both tiles completed
 constexpr int kTiles = 2;             // Q tiles per CTA, 128 rows each
 constexpr int kNodesPerTile = 16;
 constexpr int kNodesPerCta = kTiles * kNodesPerTile;
@@ -78,7 +78,7 @@ constexpr uint32_t kOffK = kTiles * 2 * kQHalf;              // K slots
 constexpr uint32_t kOffV = kOffK + kKStages * kSlotBytes;    // V slots
 constexpr uint32_t kOffBar = kOffV + kVStages * kSlotBytes;  // 229376
 constexpr uint32_t kSmemBytes = kOffBar + 512 + 1024;
-// TMEM (512 columns): one S buffer shared by the tiles, O[tile], Q[tile] (bf16 pairs)
+// TMEM (512 columns): one S buffer shared by the tiles, O[tile], P[tile] (bf16 pairs)
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColO = 128, kColP = 384;  // P of tile t: 64 columns of bf16 pairs
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
