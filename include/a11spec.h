@@ -220,7 +220,8 @@ int a11s_accept_static(int32_t mode, int32_t dtype,
  * the row's bf16 logits in the chunk and the first position holding it,
  * packed for a11s_accept_recorded, which then takes its chunk records from
  * them and never streams the logits for them. -0 counts as +0 and a NaN as
- * the largest value.
+ * the largest value. The call clears chunk_keys on `stream` before the
+ * kernel fills them, so the caller need not initialise them.
  * workspace >= 256 bytes (status word: A11S_ETIMEOUT if a pipeline wait of the
  * kernel ran out).
  */
