@@ -841,11 +841,22 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // the sampling modes), one per warp, so every root is recorded in the first
     // wave by many SMs at once. (root_blocks = 0 only in GREEDY with chunk
     // keys, whose records are all written before the launch.) The rows after
-    // them take the other units in slices.
+    // them take the other units in slices. A small GREEDY pass runs as one
+    // wave instead (a.rr > 0), with no root blocks.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
-    int u0 = 0, u1 = 0;
-    if (blockIdx.y == 0 && a.root_blocks == 0) {
+    int u0 = 0, u1 = 0, ustep = kWarps;
+    if (a.rr > 0) {
+        // One wave (a small pass): rows 1 .. rr take unit u on row
+        // 1 + (u / kWarps) % rr, warp u % kWarps, so the units finish in their
+        // order: the roots first, then the rows in index order, while every
+        // block lives for the whole pass.
+        if (blockIdx.y >= 1) {
+            u0 = (blockIdx.y - 1) * kWarps;
+            u1 = a.units_per_seq;
+            ustep = a.rr * kWarps;
+        }
+    } else if (blockIdx.y == 0 && a.root_blocks == 0) {
         // without root blocks the walker records its root itself; with chunk
         // keys every record is written before the launch
         u1 = a.keys ? 0 : n_root_units;
@@ -857,7 +868,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         u1 = min(u0 + a.slice, a.units_per_seq);
     }
     int bad = 0;
-    for (int u = u0 + warp; u < u1; u += kWarps) {
+    for (int u = u0 + warp; u < u1; u += ustep) {
         int j, r;
         if (u < n_root_units) {
             j = u / kRootRows;

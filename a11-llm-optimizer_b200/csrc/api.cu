@@ -4,6 +4,7 @@
 // device memory or synchronises a stream (except a11s_read_status, documented
 // as synchronising).
 #include <cmath>
+#include <algorithm>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -35,6 +36,7 @@ inline bool aligned16(const void *p) { return (reinterpret_cast<uintptr_t>(p) & 
 inline size_t up256(size_t x) { return (x + 255) & ~size_t(255); }
 
 constexpr size_t kHeaderBytes = 256;  // status word lives at offset 0
+constexpr long long kOneWaveRounds = 64;  // chunks per warp up to which a GREEDY pass runs as one wave
 
 int sm_count() {
     static int n = 0;
@@ -201,6 +203,20 @@ int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.slice = (int32_t)slice;
     // with chunk keys there is nothing to stream: the walkers and the root blocks
     int grid_y = 1 + a.root_blocks + (keys ? 0 : (int)((rest + slice - 1) / slice));
+    // A small GREEDY pass (at most kOneWaveRounds chunks per warp) runs as one
+    // wave instead: the walker and rr streaming blocks per sequence, all
+    // resident at once, taking the units round-robin (roots first, then the
+    // rows in index order). Blocks that stream one chunk per warp live about
+    // one memory round trip, and the block scheduler then keeps only about
+    // 60 % of the slots busy.
+    a.rr = 0;
+    const long long rr = ((long long)sm_count() * 2 - batch) / batch;
+    if (mode == A11S_ACCEPT_GREEDY && !keys && rr >= 1 &&
+        (a.units_per_seq + rr * 16 - 1) / (rr * 16) <= kOneWaveRounds) {
+        a.rr = (int32_t)std::min<long long>(rr, (a.units_per_seq + 15) / 16);
+        a.root_blocks = 0;
+        grid_y = 1 + a.rr;
+    }
     a.bulk_rows = grid_y;
     if (mode != A11S_ACCEPT_GREEDY) {
         // Helper rows: blocks scheduled after every walking and streaming block
