@@ -13,20 +13,28 @@
 // its chunk records instead of streaming the logits once more.
 // Semantics: include/a11spec.h (a11s_lm_head).
 //
-// Persistent kernel, one CTA per SM, tiles of 128 rows x 256 vocabulary
-// entries taken m-fastest, so the CTAs at work at one time share a weight tile
-// (read from HBM once) and the hidden states stay in L2. 192 threads:
-//   warp 0     TMA producer: K slices of 64 of the hidden tile (128 x 64) and
-//              the weight tile (256 x 64) into a 4-stage ring, 128-byte swizzle
-//   warp 1     TMEM allocator and MMA issuer: per K slice 4 x tcgen05.mma
-//              M128 N256 K16, both operands K-major in shared memory, into one
-//              of two accumulators of 256 TMEM columns
+// Persistent kernel of CTA pairs (clusters of 2, one CTA per SM), tiles of
+// 256 rows x 256 vocabulary entries taken m-fastest, so the pairs at work at
+// one time share a weight tile (read from HBM once) and the hidden states stay
+// in L2. Each CTA stages its own 128 rows of the hidden tile and its half (128
+// rows) of the weight tile; the even CTA issues cta_group::2 MMAs over both,
+// and each CTA's TMEM holds its 128 rows of the accumulator. Against single
+// CTAs with 128 x 256 tiles this moves a third less operand data per SM
+// through shared memory. 192 threads per CTA:
+//   warp 0     TMA producer: K slices of 64 of its hidden rows (128 x 64) and
+//              weight rows (128 x 64) into a 6-stage ring, 128-byte swizzle;
+//              both CTAs' copies complete on the even CTA's barrier
+//   warp 1     TMEM allocator (both CTAs) and, in the even CTA, MMA issuer:
+//              per K slice 4 x tcgen05.mma.cta_group::2 M256 N256 K16, both
+//              operands K-major in shared memory, into one of two accumulators
+//              of 256 TMEM columns; commits signal both CTAs
 //   warps 2-5  epilogue (thread = tile row = TMEM lane): 128 columns per TMEM
 //              load, bf16 rounding (nearest even), the chunk key on packed
 //              pairs, the bf16 tile staged in swizzled shared memory and
 //              written by TMA stores (clipped at the vocabulary and the last
-//              row). The accumulator is released after its last load, so the
-//              epilogue of tile i runs under the MMAs of tile i + 1.
+//              row). The accumulator is released (to the even CTA) after its
+//              last load, so the epilogue of tile i runs under the MMAs of
+//              tile i + 1.
 // Every mbarrier wait is bounded; a timeout sets ETIMEOUT, and the CTA drains
 // its copies and MMAs and returns.
 #include <cuda.h>
@@ -42,22 +50,27 @@
 namespace a11s {
 
 namespace {
-constexpr int kBM = 128, kBN = 256, kBK = 64;
-constexpr int kStages = 4;
-constexpr uint32_t kABytes = kBM * kBK * 2;               // 16 KB
-constexpr uint32_t kBBytes = kBN * kBK * 2;               // 32 KB
-constexpr uint32_t kStageBytes = kABytes + kBBytes;       // 48 KB
-constexpr uint32_t kBoxBytes = 32 * 128;                  // one stored box: 32 rows x 64 columns
-constexpr uint32_t kStageWarpBytes = 2 * kBoxBytes;       // an epilogue warp's staging area
-constexpr uint32_t kOffStage = kStages * kStageBytes;     // 196608
-constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarpBytes;
-constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;     // + barriers + alignment slack
-static_assert(kSmemBytes <= 232448, "shared memory budget");
+constexpr int kBM = 128, kBN = 256, kBK = 64;  // a CTA's tile rows, tile columns, K slice
+constexpr uint32_t kABytes = kBM * kBK * 2;    // 16 KB
+constexpr uint32_t kBoxBytes = 32 * 128;       // one stored box: 32 rows x 64 columns
+constexpr uint32_t kStageWarpBytes = 2 * kBoxBytes;  // an epilogue warp's staging area
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 2 * kBN;
-constexpr uint32_t kIdesc = tc::idesc_bf16_f32(kBM, kBN, false);
 constexpr long long kWaitBudget = 2000000000ll;  // ~1 s of SM clock
 static_assert(A11S_CHUNK % kBN == 0, "a tile lies inside one chunk");
+// A CTA pair (cluster of 2, cta_group::2 MMAs issued by the even CTA) computes
+// 256 x 256 tiles: each CTA stages its 128 hidden rows and half of the weight
+// tile (128 x 64 per K slice: 32 KB stages), and its TMEM holds its 128 rows
+// of the accumulator.
+constexpr int kStages = 6;
+constexpr int kTileRows = 2 * kBM;
+constexpr uint32_t kBRows = kBN / 2;  // weight rows a CTA stages
+constexpr uint32_t kStageBytes = kABytes + kBRows * kBK * 2;
+constexpr uint32_t kOffStage = kStages * kStageBytes;  // 196608
+constexpr uint32_t kOffBar = kOffStage + 4 * kStageWarpBytes;
+constexpr uint32_t kSmemBytes = kOffBar + 256 + 1024;  // + barriers + alignment slack
+constexpr uint32_t kIdesc = tc::idesc_bf16_f32(kTileRows, kBN, false);
+static_assert(kSmemBytes <= 232448, "shared memory budget");
 
 struct Bars {
     uint64_t full[kStages], empty[kStages];
@@ -156,8 +169,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t *sm = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     Bars *bs = reinterpret_cast<Bars *>(sm + kOffBar);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // both CTAs of a pair take the same tiles
+    const uint32_t rank = tc::cluster_rank();
+    const int unit = (int)tc::cluster_id(), units = (int)tc::cluster_count();
     const int total = p.m_tiles * p.n_tiles;
-    const int my_tiles = (int)blockIdx.x < total ? (total - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+    const int my_tiles = unit < total ? (total - 1 - unit) / units + 1 : 0;
     if (my_tiles == 0) return;
 
     if (threadIdx.x == 0) {
@@ -167,23 +183,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&bs->acc_full[b], 1);
-            tc::mbar_init(&bs->acc_empty[b], 4);  // one arrival per epilogue warp
+            tc::mbar_init(&bs->acc_empty[b], 8);  // one arrival per epilogue warp of both CTAs
         }
         tc::mbar_init(&bs->drain, 1);
         bs->abort = 0;
         tc::fence_barrier_init();
     }
     if (warp == 1) {
-        tc::tmem_alloc(&bs->tmem_base, kTmemCols);
-        tc::tmem_relinquish();
+        tc::tmem_alloc_pair(&bs->tmem_base, kTmemCols);
+        tc::tmem_relinquish_pair();
     }
     tc::tc_fence_before();
-    __syncthreads();
+    tc::cluster_sync();  // the even CTA's barriers are ready before the peer signals them
     tc::tc_fence_after();
     const uint32_t tmem = bs->tmem_base;
 
     if (warp == 0) {
-        // ---------------- TMA producer ----------------
+        // ---------------- TMA producer (each CTA its own rows) ----------------
         if (lane == 0) {
             tc::prefetch_tmap(&ta);
             tc::prefetch_tmap(&tb);
@@ -191,8 +207,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             int it = 0;  // K slices issued
             bool ok = true;
             for (int i = 0; i < my_tiles && ok; ++i) {
-                const int t = (int)blockIdx.x + i * (int)gridDim.x;
-                const int m0 = (t % p.m_tiles) * kBM, n0 = (t / p.m_tiles) * kBN;
+                const int t = unit + i * units;
+                const int m0 = (t % p.m_tiles) * kTileRows + (int)rank * kBM, n0 = (t / p.m_tiles) * kBN;
                 for (int kb = 0; kb < p.k_blocks; ++kb) {
                     const int s = it % kStages, use = it / kStages;
                     // the slot was last read by the MMAs of slice it - kStages
@@ -202,21 +218,19 @@ __global__ void __launch_bounds__(kThreads, 1)
                         break;
                     }
                     uint8_t *sa = sm + s * kStageBytes;
-                    tc::mbar_arrive_expect_tx(&bs->full[s], kStageBytes);
-                    tc::tma_load_2d(sa, &ta, &bs->full[s], kb * kBK, m0);
-                    tc::tma_load_2d(sa + kABytes, &tb, &bs->full[s], kb * kBK, n0);
+                    // both CTAs' copies complete on the even CTA's barrier, which the MMAs wait on
+                    const uint32_t fb = tc::cluster_addr(&bs->full[s], 0);
+                    if (rank == 0) tc::mbar_arrive_expect_tx(&bs->full[s], 2 * kStageBytes);
+                    tc::tma_load_2d_pair(sa, &ta, fb, kb * kBK, m0);
+                    tc::tma_load_2d_pair(sa + kABytes, &tb, fb, kb * kBK, n0 + (int)(rank * kBRows));
                     ++it;
                 }
-            }
-            if (!ok) {  // copies that may still be landing in this CTA's shared memory
-                for (int j = max(0, it - kStages); j < it; ++j)
-                    tc::mbar_wait(&bs->full[j % kStages], (j / kStages) & 1, kWaitBudget);
             }
         }
         __syncwarp();
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        if (lane == 0) {
+        // ---------------- MMA issuer (the even CTA) ----------------
+        if (lane == 0 && rank == 0) {
             int it = 0;
             bool ok = true;
             for (int i = 0; i < my_tiles && ok; ++i) {
@@ -231,17 +245,18 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc::tc_fence_after();
                     const uint32_t a_addr = tc::smem_u32(sm + s * kStageBytes), b_addr = a_addr + kABytes;
 #pragma unroll
-                    for (int kk = 0; kk < kBK / 16; ++kk)
-                        tc::mma_bf16_ss(d, tc::sdesc_sw128(a_addr + kk * 32, 16, 1024),
-                                        tc::sdesc_sw128(b_addr + kk * 32, 16, 1024), kIdesc,
-                                        (kb | kk) != 0 ? 1u : 0u);
-                    tc::mma_commit(&bs->empty[s]);
+                    for (int kk = 0; kk < kBK / 16; ++kk) {
+                        const uint64_t ad = tc::sdesc_sw128(a_addr + kk * 32, 16, 1024);
+                        const uint64_t bd = tc::sdesc_sw128(b_addr + kk * 32, 16, 1024);
+                        tc::mma_bf16_ss_pair(d, ad, bd, kIdesc, (kb | kk) != 0 ? 1u : 0u);
+                    }
+                    tc::mma_commit_pair_both(&bs->empty[s]);
                     ++it;
                 }
-                if (ok) tc::mma_commit(&bs->acc_full[buf]);
+                if (ok) tc::mma_commit_pair_both(&bs->acc_full[buf]);
             }
-            // every issued MMA completes before the CTA may release TMEM
-            tc::mma_commit(&bs->drain);
+            // every issued MMA completes before either CTA may release TMEM or shared memory
+            tc::mma_commit_pair(&bs->drain);
             tc::mbar_wait(&bs->drain, 0, kWaitBudget);
         }
         __syncwarp();
@@ -255,8 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t srow = tc::smem_u32(stage) + (uint32_t)lane * 128u;
         bool ok = true;
         for (int i = 0; i < my_tiles && ok; ++i) {
-            const int t = (int)blockIdx.x + i * (int)gridDim.x;
-            const int m0 = (t % p.m_tiles) * kBM, n0 = (t / p.m_tiles) * kBN;
+            const int t = unit + i * units;
+            const int m0 = (t % p.m_tiles) * kTileRows + (int)rank * kBM, n0 = (t / p.m_tiles) * kBN;
             const int buf = i & 1;
             if (!(ok = __all_sync(0xffffffffu, wait_or_abort(&bs->acc_full[buf], (i >> 1) & 1, bs, p.status)))) break;
             tc::tc_fence_after();
@@ -273,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (half == 1) {  // the accumulator is in registers: the next tile may use it
                         tc::tc_fence_before();
                         __syncwarp();
-                        if (lane == 0) tc::mbar_arrive(&bs->acc_empty[buf]);
+                        if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&bs->acc_empty[buf], 0));
                     }
 #pragma unroll
                     for (int e = 0; e < 64; ++e)
@@ -308,11 +323,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) tc::bulk_wait_all();
         __syncwarp();
     }
+    // After a timeout copies may still be landing here, and their completion
+    // is counted on the even CTA's barrier: give them time (about 0.2 ms)
+    // before the shared memory is released.
+    if (threadIdx.x == 0 && aborted(bs)) {
+        const long long t0 = clock64();
+        while (clock64() - t0 < 400000) {
+        }
+    }
     tc::tc_fence_before();
-    __syncthreads();
+    tc::cluster_sync();  // the pair's MMAs and remote arrivals are over
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, kTmemCols);
+        tc::tmem_dealloc_pair(tmem, kTmemCols);
     }
 }
 
@@ -345,12 +368,22 @@ bool encode_rows(CUtensorMap *map, const void *base, int64_t inner, int64_t oute
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
+
+// Clusters of two that can be resident at once (one CTA per SM).
+int lm_pair_slots(const cudaLaunchConfig_t &cfg, int sms) {
+    static int n = 0;
+    if (!n) {
+        int c = 0;
+        n = cudaOccupancyMaxActiveClusters(&c, lm_head_tc, &cfg) == cudaSuccess && c > 0 ? c : sms / 2;
+    }
+    return n;
+}
 }  // namespace
 
 cudaError_t launch_lm_head(const LmHeadArgs &a, cudaStream_t s) {
     CUtensorMap ta, tb;
     if (!encode_rows(&ta, a.hidden, a.K, a.rows, kBM)) return cudaErrorInvalidValue;
-    if (!encode_rows(&tb, a.weight, a.K, a.V, kBN)) return cudaErrorInvalidValue;
+    if (!encode_rows(&tb, a.weight, a.K, a.V, kBRows)) return cudaErrorInvalidValue;
     CUtensorMap to;  // logits [rows][V] with row pitch ldl: 64 x 32 boxes, 128-byte swizzle
     if (!encode_rows(&to, a.logits, a.V, a.rows, 32, a.ldl)) return cudaErrorInvalidValue;
     cudaError_t e = cudaFuncSetAttribute(lm_head_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
@@ -363,7 +396,7 @@ cudaError_t launch_lm_head(const LmHeadArgs &a, cudaStream_t s) {
     p.rows = a.rows;
     p.V = a.V;
     p.nch = (a.V + A11S_CHUNK - 1) / A11S_CHUNK;
-    p.m_tiles = (a.rows + kBM - 1) / kBM;
+    p.m_tiles = (a.rows + kTileRows - 1) / kTileRows;
     p.n_tiles = (a.V + kBN - 1) / kBN;
     p.k_blocks = (int32_t)((a.K + kBK - 1) / kBK);
     p.status = a.status;
@@ -373,10 +406,23 @@ cudaError_t launch_lm_head(const LmHeadArgs &a, cudaStream_t s) {
     }
     int sms = 148, dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long tiles = (long long)p.m_tiles * p.n_tiles;
-    const int grid = (int)std::min<long long>(tiles, sms);
-    lm_head_tc<<<grid, kThreads, kSmemBytes, s>>>(ta, tb, to, p);
-    return cudaGetLastError();
+    // persistent: one CTA pair per two SMs (clusters of 2), at most one pair per tile
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(2 * (sms / 2));
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = kSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    const long long pairs = std::min<long long>((long long)p.m_tiles * p.n_tiles, lm_pair_slots(cfg, sms));
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    return cudaLaunchKernelEx(&cfg, lm_head_tc, ta, tb, to, p);
 }
+
 
 }  // namespace a11s
