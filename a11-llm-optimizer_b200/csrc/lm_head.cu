@@ -100,17 +100,12 @@ __device__ __forceinline__ bool wait_or_abort(uint64_t *bar, uint32_t parity, Ba
 }
 }  // namespace
 
-// Order-preserving images of a bf16 pair for an unsigned maximum, per half:
-// sign set -> all 16 bits flipped, else the sign bit set. -0 (0x7FFF) then
-// sits just below +0 (0x8000); the key treats them as equal (below).
+// Order-preserving images of a bf16 pair for an unsigned comparison, per
+// half: sign set -> all 16 bits flipped, else the sign bit set (+0 -> 0x8000,
+// -inf -> 0x007F).
 __device__ __forceinline__ uint32_t lm_order2(uint32_t w) {
     const uint32_t s = (w >> 15) & 0x00010001u;
     return w ^ (s * 0x7FFFu + 0x80008000u);
-}
-__device__ __forceinline__ uint32_t lm_max_u16x2(uint32_t a, uint32_t b) {
-    uint32_t d;
-    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
-    return d;
 }
 __device__ __forceinline__ uint32_t lm_max_nan_bf16x2(uint32_t a, uint32_t b) {
     uint32_t d;
@@ -119,47 +114,49 @@ __device__ __forceinline__ uint32_t lm_max_nan_bf16x2(uint32_t a, uint32_t b) {
 }
 
 // Chunk key of 128 columns (col0 .. col0 + 127 of the tile; w = their bf16
-// pairs) folded into (best, best_col): the largest ordered value, -0 taken as
-// +0 and any NaN as the largest (0xFFFF), and the first column holding it.
-// Columns at or past `valid` take no part. A later half replaces the best
-// only when strictly larger, so the first position wins ties.
-__device__ __forceinline__ void lm_half_key(const uint32_t (&w)[64], int col0, int valid, uint32_t &best,
-                                            int &best_col) {
-    uint32_t o[64];
-    uint32_t mx = 0, nan = 0;
-#pragma unroll
-    for (int e = 0; e < 64; ++e) {
-        o[e] = lm_order2(w[e]);
-        nan = lm_max_nan_bf16x2(nan, w[e]);
-    }
-    if ((nan & 0x7FFFu) > 0x7F80u || (nan >> 16 & 0x7FFFu) > 0x7F80u) {  // a NaN: it is the maximum
-#pragma unroll
-        for (int e = 0; e < 64; ++e) {
-            if ((w[e] & 0x7FFFu) > 0x7F80u) o[e] |= 0xFFFFu;
-            if ((w[e] >> 16 & 0x7FFFu) > 0x7F80u) o[e] |= 0xFFFF0000u;
-        }
-    }
+// pairs, already staged for the store) folded into (best, best_col): the
+// largest ordered value, -0 taken as +0 and any NaN as the largest (0xFFFF),
+// and the first column holding it. Columns at or past `valid` take no part
+// (set to -inf here; the store clips them). The maximum is one packed
+// NaN-propagating chain; the position is searched only when this half beats
+// `best`, which a later half must strictly exceed, so the first position wins
+// ties.
+__device__ __forceinline__ void lm_half_key(uint32_t (&w)[64], int col0, int valid, uint32_t &best, int &best_col) {
     if (col0 + 128 > valid) {  // the vocabulary ends in this half (valid is a multiple of 8)
 #pragma unroll
         for (int e = 0; e < 64; ++e)
-            if (col0 + 2 * e >= valid) o[e] = 0u;
+            if (col0 + 2 * e >= valid) w[e] = 0xFF80FF80u;
     }
+    uint32_t mx = w[0];
 #pragma unroll
-    for (int e = 0; e < 64; ++e) mx = lm_max_u16x2(mx, o[e]);
-    uint32_t M = max(mx & 0xFFFFu, mx >> 16);
-    if (M == 0x7FFFu) M = 0x8000u;  // a zero maximum: -0 counts as +0
-    if (M > best) {
-        const uint32_t Mz = M == 0x8000u ? 0x7FFFu : M;  // and matches either sign
-        int pos = 0;
+    for (int e = 1; e < 64; ++e) mx = lm_max_nan_bf16x2(mx, w[e]);
+    const uint32_t lo = mx & 0xFFFFu, hi = mx >> 16;
+    int pos = 0;
+    if ((lo & 0x7FFFu) > 0x7F80u || (hi & 0x7FFFu) > 0x7F80u) {  // a NaN: it is the maximum
+        if (0xFFFFu <= best) return;
 #pragma unroll
         for (int e = 63; e >= 0; --e) {
-            const uint32_t lo = o[e] & 0xFFFFu, hi = o[e] >> 16;
-            if (hi == M || hi == Mz) pos = 2 * e + 1;
-            if (lo == M || lo == Mz) pos = 2 * e;
+            if ((w[e] >> 16 & 0x7FFFu) > 0x7F80u) pos = 2 * e + 1;
+            if ((w[e] & 0x7FFFu) > 0x7F80u) pos = 2 * e;
         }
-        best = M;
+        best = 0xFFFFu;
         best_col = col0 + pos;
+        return;
     }
+    // the larger of the two halves (no NaN left), a zero maximum as +0
+    uint32_t Mv = __uint_as_float(lo << 16) >= __uint_as_float(hi << 16) ? lo : hi;
+    if ((Mv & 0x7FFFu) == 0) Mv = 0;
+    const uint32_t M = lm_order2(Mv) & 0xFFFFu;
+    if (M <= best) return;
+    const uint32_t Mz = Mv == 0 ? 0x8000u : Mv;  // a zero maximum matches either sign
+#pragma unroll
+    for (int e = 63; e >= 0; --e) {
+        const uint32_t l = w[e] & 0xFFFFu, h = w[e] >> 16;
+        if (h == Mv || h == Mz) pos = 2 * e + 1;
+        if (l == Mv || l == Mz) pos = 2 * e;
+    }
+    best = M;
+    best_col = col0 + pos;
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
@@ -294,7 +291,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int e = 0; e < 64; ++e)
                         w[e] = tc::cvt_bf16x2(__fmul_rn(v[2 * e], p.scale), __fmul_rn(v[2 * e + 1], p.scale));
                 }
-                if (p.keys && half * 128 < valid) lm_half_key(w, half * 128, valid, best, best_col);
                 // the previous stores from the staging area have read it
                 if (lane == 0) tc::bulk_wait_read_all();
                 __syncwarp();
@@ -313,6 +309,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     tc::tma_store_2d(&tc_out, stage + kBoxBytes, n0 + half * 128 + 64, m0 + q * 32);
                     tc::bulk_commit_group();
                 }
+                if (p.keys && half * 128 < valid) lm_half_key(w, half * 128, valid, best, best_col);
             }
             if (p.keys && row < p.rows && valid > 0) {
                 const int pos = (n0 % A11S_CHUNK) + best_col;
