@@ -287,9 +287,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         __syncwarp();
                         if (lane == 0) tc::mbar_arrive_cluster(tc::cluster_addr(&bs->acc_empty[buf], 0));
                     }
+                    if (p.scale == 1.0f) {  // uniform: bf16_rn(1 * x) is bf16_rn(x)
 #pragma unroll
-                    for (int e = 0; e < 64; ++e)
-                        w[e] = tc::cvt_bf16x2(__fmul_rn(v[2 * e], p.scale), __fmul_rn(v[2 * e + 1], p.scale));
+                        for (int e = 0; e < 64; ++e) w[e] = tc::cvt_bf16x2(v[2 * e], v[2 * e + 1]);
+                    } else {  // two products per instruction, each rounded to nearest
+#pragma unroll
+                        for (int e = 0; e < 64; ++e) {
+                            const float2 sv = tc::fmul2(make_float2(v[2 * e], v[2 * e + 1]), make_float2(p.scale, p.scale));
+                            w[e] = tc::cvt_bf16x2(sv.x, sv.y);
+                        }
+                    }
                 }
                 // the previous stores from the staging area have read it
                 if (lane == 0) tc::bulk_wait_read_all();
