@@ -1207,18 +1207,16 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                         if (!ex) {
                             __syncwarp();
                             if (lane == 0) {
+                                // S_eff = sum_j sub[j] >> (C - fr[j]) (as combine_sums
+                                // forms S); only chunk j's term changes
                                 sm.excl[sm.nexcl++] = x;
-                                if (sm.fr[j] != A11S_FRAME_NONE) sm.sub[j] -= det_weight(sm.kl[kk], a.k, (float)sm.fr[j]);
+                                if (sm.fr[j] != A11S_FRAME_NONE) {
+                                    const int d = sm.ps.C - sm.fr[j];
+                                    const uint64_t before = d > 63 ? 0ull : (sm.sub[j] >> d);
+                                    sm.sub[j] -= det_weight(sm.kl[kk], a.k, (float)sm.fr[j]);
+                                    sm.S_eff = sm.S_eff - before + (d > 63 ? 0ull : (sm.sub[j] >> d));
+                                }
                             }
-                            __syncwarp();
-                            uint64_t S = 0;  // warp-parallel renormalisation
-                            for (int jj = lane; jj < nch; jj += 32) {
-                                if (sm.fr[jj] == A11S_FRAME_NONE) continue;
-                                const int d = sm.ps.C - sm.fr[jj];
-                                S += d > 63 ? 0ull : (sm.sub[jj] >> d);
-                            }
-                            S = warp_sum_u64(S);
-                            if (lane == 0) sm.S_eff = S;
                             __syncwarp();
                         }
                     }
