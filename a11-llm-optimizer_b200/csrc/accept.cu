@@ -615,25 +615,21 @@ __device__ void pass_chunk(const AcceptArgs &a, int b, int kind, int node, int L
     }
 }
 
-// Take chunks of the walks' open passes, one warp at a time (sampling modes).
-// Lane 0 looks for an open pass with an unclaimed chunk, starting at a
-// sequence of its own, and claims one chunk; the warp computes it. A pass's
-// parameters were written before it was opened; they are read from L2 after
-// the claim. Helper blocks (grid rows >= bulk_rows) keep looking until every
-// walk has finished (or their budget ran out); a streaming block that has
-// finished its own units leaves as soon as a scan finds nothing open.
+// Take chunks of the walks' open passes, one warp at a time (sampling modes;
+// the helper blocks, grid rows >= bulk_rows). Lane 0 looks for an open pass
+// with an unclaimed chunk, starting at a sequence of its own, and claims one
+// chunk; the warp computes it. A pass's parameters were written before it was
+// opened; they are read from L2 after the claim. The warps keep looking until
+// every walk has finished (or their budget ran out). Streaming blocks do not
+// help: their pass chunks (compute-heavy) held back the bulk pass, which is
+// the longer of the two at C3 (907-909 us with their help, 882-892 without).
 template <int MODE, bool BF16>
-__device__ void help_passes(const AcceptArgs &a, int warp, int lane, bool until_walks_end, double *invT) {
+__device__ void help_passes(const AcceptArgs &a, int warp, int lane, double *invT) {
     const long long t0 = clock64();
     int start = (int)((blockIdx.y * gridDim.x + blockIdx.x) * kWarps + warp) % a.B;
     for (;;) {
         int b = -1, j = -1;
-        bool leave = false;
-        if (until_walks_end) {
-            leave = ld_relaxed(a.walkers_done) >= (uint32_t)a.B || clock64() - t0 > kHelperBudget;
-        } else {
-            leave = ld_relaxed(a.open_passes) == 0;  // one load: nothing open, a streaming block leaves
-        }
+        bool leave = ld_relaxed(a.walkers_done) >= (uint32_t)a.B || clock64() - t0 > kHelperBudget;
         leave = __shfl_sync(0xffffffffu, leave, 0);
         if (leave) return;
         // the lanes read 32 sequences' pass words at once; lane 0 claims from
@@ -657,7 +653,6 @@ __device__ void help_passes(const AcceptArgs &a, int warp, int lane, bool until_
             }
         }
         if (j < 0) {
-            if (!until_walks_end) return;  // a streaming block does not wait for passes
             __nanosleep(256);
             continue;
         }
@@ -823,7 +818,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // returns at once.
     asm volatile("griddepcontrol.wait;" ::: "memory");
     if ((int)blockIdx.y >= a.bulk_rows) {  // helper block (sampling modes only)
-        if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, true, s_invT[warp]);
+        if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, s_invT[warp]);
         return;
     }
     int n_live = a.n_nodes ? a.n_nodes[b] : a.N;
@@ -912,11 +907,7 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         }
     }
     if (warp_or(bad) && lane == 0) report(a.status, A11S_ENONFINITE, b);
-    if (blockIdx.y != 0) {
-        // a streaming block that is done takes chunks of open walk passes before it leaves
-        if constexpr (MODE != A11S_ACCEPT_GREEDY) help_passes<MODE, BF16>(a, warp, lane, false, s_invT[warp]);
-        return;
-    }
+    if (blockIdx.y != 0) return;  // a streaming block is done
 
     // ---------------- phase 2: walk ----------------
     __shared__ WalkSmem sm;
@@ -987,7 +978,6 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         __syncthreads();
         if (threadIdx.x == 0) {
             sm.gen += 1;
-            atomicAdd(a.open_passes, 1);  // streaming blocks that finish look for open passes
             atomicExch(&job->word, (unsigned long long)sm.gen << 32);  // open the pass
         }
         __syncthreads();
@@ -1015,7 +1005,6 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
                 atomicExch(&job->word, ((unsigned long long)gen << 32) | kClosedCount);
                 sm.no_helpers = 1;
             }
-            atomicSub(a.open_passes, 1);
             __threadfence();
         }
         __syncthreads();
@@ -1421,7 +1410,7 @@ __global__ void accept_keys_init_kernel(const AcceptArgs a, int mode, uint4 *zer
     const size_t i0 = (size_t)blockIdx.x * blockDim.x + threadIdx.x, step = (size_t)gridDim.x * blockDim.x;
     if (i0 == 0) {
         *a.status = StatusWord{};
-        reinterpret_cast<uint4 *>(a.status)[1] = make_uint4(0, 0, 0, 0);  // the walk counters at bytes 16 and 20
+        reinterpret_cast<uint4 *>(a.status)[1] = make_uint4(0, 0, 0, 0);  // the finished-walk counter at byte 16
     }
     for (size_t i = i0; i < z16; i += step) zero[i] = make_uint4(0, 0, 0, 0);
     // records [B][N][nch] (rows_per_seq == N in GREEDY and STOCH_ONEHOT), the keys in the same order

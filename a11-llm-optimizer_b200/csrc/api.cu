@@ -175,8 +175,7 @@ int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.recs = reinterpret_cast<float *>(ws + L.recs);
     a.arg = mode == A11S_ACCEPT_GREEDY ? reinterpret_cast<int32_t *>(ws + L.arg) : nullptr;
     a.root_sums = reinterpret_cast<unsigned long long *>(ws + L.root_sums);
-    a.walkers_done = reinterpret_cast<int32_t *>(ws + 16);  // header: status word at 0, counters at 16 and 20
-    a.open_passes = reinterpret_cast<int32_t *>(ws + 20);
+    a.walkers_done = reinterpret_cast<int32_t *>(ws + 16);  // header: status word at 0, the finished-walk counter at 16
     a.jobs = mode == A11S_ACCEPT_GREEDY ? nullptr : ws + L.jobs;
     a.job_stride = (int64_t)a11s::accept_job_bytes(a.nch);
     // A walking block may wait for rows that other blocks record only when the

@@ -37,7 +37,6 @@ struct AcceptArgs {
     char *jobs;
     int64_t job_stride;
     int32_t *walkers_done;
-    int32_t *open_passes;  // passes published and not yet complete
     int32_t bulk_rows;    // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
     int32_t root_blocks;  // grid rows 1 .. root_blocks take the root units, one per warp (0: the walker does)
     int32_t rr;           // > 0: one wave, grid rows 1 .. rr take every unit round-robin (slice, root_blocks unused)

@@ -173,11 +173,16 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sm)}
 
 
-def device_time_us(fn, iters: int, pre=None) -> float:
+def device_time_us(fn, iters: int, pre=None, warmup: int = 1) -> float:
     """Mean device time of fn(i) over `iters` launches, each between its own
-    pair of CUDA events on the current stream. A GPU-side spin queued first
-    keeps the device busy while the host enqueues every launch, so host launch
-    overhead never shows up as device time. pre(i) runs outside the events."""
+    pair of CUDA events on the current stream, after `warmup` untimed launches
+    (fn(0)). A GPU-side spin queued first keeps the device busy while the host
+    enqueues every launch, so host launch overhead never shows up as device
+    time. pre(i) runs outside the events."""
+    for _ in range(warmup):
+        if pre is not None:
+            pre(0)
+        fn(0)
     torch.cuda.synchronize()
     torch.cuda._sleep(100_000_000)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(iters)]
