@@ -831,13 +831,14 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
     // root in DRAFT mode), then the other rows in index order (in DRAFT mode
     // p row i then q row i), a row's chunks consecutive, so the rows near the
     // root, which the walk visits first, are recorded first. Grid row 0 is the
-    // sequence's walker and streams nothing; rows 1 .. root_blocks take the
+    // sequence's walker and streams nothing; root_blocks root rows take the
     // root units (chunk maxima, and first positions in GREEDY or weight sums in
-    // the sampling modes), one per warp, so every root is recorded in the first
-    // wave by many SMs at once. (root_blocks = 0 only in GREEDY with chunk
-    // keys, whose records are all written before the launch.) The rows after
-    // them take the other units in slices. A small GREEDY pass runs as one
-    // wave instead (a.rr > 0), with no root blocks.
+    // the sampling modes), one per warp, so every root is recorded early by
+    // many SMs at once. (root_blocks = 0 only in GREEDY with chunk keys, whose
+    // records are all written before the launch.) The streaming rows take the
+    // other units in slices; the root rows alternate with the first of them.
+    // A small GREEDY pass runs as one wave instead (a.rr > 0), with no root
+    // blocks.
     constexpr int kRootRows = MODE == A11S_ACCEPT_STOCH_DRAFT ? 2 : 1;
     const int n_root_units = kRootRows * a.nch;
     int u0 = 0, u1 = 0, ustep = kWarps;
@@ -855,12 +856,23 @@ __global__ void __launch_bounds__(kThreads, 2) accept_kernel(const AcceptArgs a)
         // without root blocks the walker records its root itself; with chunk
         // keys every record is written before the launch
         u1 = a.keys ? 0 : n_root_units;
-    } else if (blockIdx.y >= 1 && (int)blockIdx.y <= a.root_blocks) {
-        u0 = (blockIdx.y - 1) * kWarps;
-        u1 = min(u0 + kWarps, n_root_units);
-    } else if ((int)blockIdx.y > a.root_blocks) {
-        u0 = n_root_units + (blockIdx.y - 1 - a.root_blocks) * a.slice;
-        u1 = min(u0 + a.slice, a.units_per_seq);
+    } else if (blockIdx.y >= 1 && (int)blockIdx.y < a.bulk_rows) {
+        // The first root_pairs root rows alternate with streaming rows (root
+        // first), so the root blocks' compute-heavy units (weight sums in the
+        // sampling modes) run beside memory-bound streaming blocks; then the
+        // other root rows, then the other streaming rows.
+        const int pairs = a.root_pairs, y = (int)blockIdx.y - 1, y2 = y - 2 * pairs;
+        int root_i = -1, slice_i = -1;
+        if (y < 2 * pairs) (y & 1 ? slice_i : root_i) = y >> 1;
+        else if (y2 < a.root_blocks - pairs) root_i = pairs + y2;
+        else slice_i = pairs + (y2 - (a.root_blocks - pairs));
+        if (root_i >= 0) {
+            u0 = root_i * kWarps;
+            u1 = min(u0 + kWarps, n_root_units);
+        } else {
+            u0 = n_root_units + slice_i * a.slice;
+            u1 = min(u0 + a.slice, a.units_per_seq);
+        }
     }
     int bad = 0;
     for (int u = u0 + warp; u < u1; u += ustep) {

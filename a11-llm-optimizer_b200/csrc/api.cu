@@ -202,6 +202,17 @@ int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const vo
     a.slice = (int32_t)slice;
     // with chunk keys there is nothing to stream: the walkers and the root blocks
     int grid_y = 1 + a.root_blocks + (keys ? 0 : (int)((rest + slice - 1) / slice));
+    // Streaming rows interleaved with the root rows: as many as the first wave
+    // holds beside the walkers and every root row. Root rows that a long-lived
+    // streaming block pushes out of the first wave start late, and so do the
+    // walks (C3, 2 x 64 x 151936 fp32 rows: 1014-1026 us interleaved against
+    // 892-898 us); at the one-hot C5 shape interleaving gave 94-95 us against
+    // 98-100 us.
+    {
+        const long long fit = (long long)sm_count() * 2 / batch - 1 - a.root_blocks;
+        a.root_pairs = (int32_t)std::max(0ll, std::min({fit, (long long)a.root_blocks,
+                                                        (long long)(grid_y - 1 - a.root_blocks)}));
+    }
     // A small GREEDY pass (at most kOneWaveRounds chunks per warp) runs as one
     // wave instead: the walker and rr streaming blocks per sequence, all
     // resident at once, taking the units round-robin (roots first, then the

@@ -39,6 +39,7 @@ struct AcceptArgs {
     int32_t *walkers_done;
     int32_t bulk_rows;    // grid rows 0 .. bulk_rows-1 walk and stream; rows beyond help (sampling modes)
     int32_t root_blocks;  // grid rows 1 .. root_blocks take the root units, one per warp (0: the walker does)
+    int32_t root_pairs;   // streaming rows interleaved with the root rows (<= root_blocks, <= streaming rows)
     int32_t rr;           // > 0: one wave, grid rows 1 .. rr take every unit round-robin (slice, root_blocks unused)
     const unsigned long long *keys;  // chunk keys of the LM head ([B * N][nch]): records come from them, no bulk pass
 };
