@@ -205,9 +205,10 @@ int accept_call(int32_t mode, int32_t dtype, const void *target_logits, const vo
     // Streaming rows interleaved with the root rows: as many as the first wave
     // holds beside the walkers and every root row. Root rows that a long-lived
     // streaming block pushes out of the first wave start late, and so do the
-    // walks (C3, 2 x 64 x 151936 fp32 rows: 1014-1026 us interleaved against
-    // 892-898 us); at the one-hot C5 shape interleaving gave 94-95 us against
-    // 98-100 us.
+    // walks (64 sequences of 64 fp32 p and q rows over 151936 tokens, 640
+    // root blocks: 1014-1026 us interleaved against 892-898 us); for 32
+    // sequences of 64 bf16 rows over 151936 tokens, one-hot, interleaving gave
+    // 94-95 us against 98-100 us.
     {
         const long long fit = (long long)sm_count() * 2 / batch - 1 - a.root_blocks;
         a.root_pairs = (int32_t)std::max(0ll, std::min({fit, (long long)a.root_blocks,
